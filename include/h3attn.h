@@ -1,0 +1,120 @@
+/* C ABI of the B200 (sm_100a) MiniMax-H3 Ulysses attention library, libh3attn.so.
+ *
+ * Plain pointers and sizes only: every tensor argument is a device pointer, every
+ * size and stride is an int64 count of ELEMENTS (bf16 unless stated), and every call
+ * takes the caller's CUDA stream as `void*` (a cudaStream_t; NULL = legacy default
+ * stream). Calls are asynchronous: they validate arguments, enqueue kernels and return.
+ * Nothing here allocates device memory; callers pass every buffer, including the
+ * int32 device status word that bounded in-kernel waits report into.
+ *
+ * Return values: 0 on success, a negative H3_ERR_* on a rejected argument or a failed
+ * launch. A kernel that gave up waiting (it never hangs the GPU) leaves a positive
+ * H3_STATUS_* code in the status word; read it with h3_status_read(). The status word
+ * must be zero before a launch; it is sticky (kernels only ever write non-zero codes).
+ *
+ * Threading: calls keep no global mutable state; distinct streams may call concurrently.
+ */
+#ifndef H3ATTN_H_
+#define H3ATTN_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define H3ATTN_VERSION 1
+
+/* return codes */
+#define H3_OK 0
+#define H3_ERR_NULL (-1)        /* a required pointer is NULL */
+#define H3_ERR_ALIGN (-2)       /* a pointer is not 16-byte aligned */
+#define H3_ERR_SHAPE (-3)       /* a size is out of range */
+#define H3_ERR_STRIDE (-4)      /* a stride is not a multiple of 8 elements / too small */
+#define H3_ERR_LAUNCH (-5)      /* the CUDA runtime refused the launch */
+#define H3_ERR_TENSOR_MAP (-6)  /* cuTensorMapEncodeTiled rejected the layout */
+#define H3_ERR_DRIVER (-7)      /* driver entry point unavailable */
+#define H3_ERR_UNSUPPORTED (-8) /* a configuration this build does not implement */
+#define H3_ERR_CUDA (-9)        /* a CUDA runtime call failed (h3_status_read) */
+
+/* device status codes (positive, written by kernels into the status word) */
+#define H3_STATUS_OK 0
+#define H3_STATUS_TIMEOUT_Q 1
+#define H3_STATUS_TIMEOUT_KV 2
+#define H3_STATUS_TIMEOUT_S 3
+#define H3_STATUS_TIMEOUT_P 4
+#define H3_STATUS_TIMEOUT_O 5
+#define H3_STATUS_TIMEOUT_DRAIN 6
+#define H3_STATUS_TIMEOUT_KAT 7
+
+/* Library build version (H3ATTN_VERSION). */
+int h3_version(void);
+
+/* Exact non-causal attention, head_dim 128, bf16 in / fp32 accumulate / bf16 out:
+ *   O[h, i, :] = softmax_j( Q[h, i, :] . K[h, j, :] * softmax_scale ) V[h, j, :],  j < s_kv
+ * Replaces the SDPA FLASH call of the Ulysses runtime, harness/sp_runtime.py:119-121
+ * (and the unwired fa3(q,k,v,o) binding, attn_sm80/fa3_sm80_h3.cu:584-593), including
+ * the pad path of sp_runtime.py:106-109: queries run over s_q rows while keys and
+ * values stop at the real length s_kv.
+ *   q: [n_heads][s_q][128] with strides (q_head_stride, q_row_stride)
+ *   k, v: [n_heads][s_kv][128] with strides (kv_head_stride, kv_row_stride)
+ *   o: row i of head h is written at
+ *        o + (i / o_rank_rows) * o_rank_stride + h * o_head_stride + (i % o_rank_rows) * o_row_stride
+ *      so one launch can write [n_heads][s_q][128], token-major [s_q][n_heads][128], or the
+ *      head->seq all-to-all send layout [world][n_heads][s_q/world][128] directly.
+ * A query row's result depends only on that row, K and V: running any subset of
+ * heads or of rows gives bit-identical rows. */
+int h3_attn_fwd(const void* q, const void* k, const void* v, void* o, int64_t n_heads, int64_t s_q, int64_t s_kv,
+                int64_t q_head_stride, int64_t q_row_stride, int64_t kv_head_stride, int64_t kv_row_stride,
+                int64_t o_rank_rows, int64_t o_rank_stride, int64_t o_head_stride, int64_t o_row_stride,
+                float softmax_scale, int32_t* status, void* stream);
+
+/* Fused per-head qk-RMSNorm + RoPE + seq->head send-buffer pack for one token shard.
+ * Replaces comfy_kitchen's in-place rms_rope_split_half_ call (harness/sp_runtime.py:93-99,
+ * or q_norm/k_norm when rope is absent, :100-101), the head transposes (:102) and the
+ * send-side reshape copy of a2a_seq_to_head (:69).
+ *   q, k, v: [s_l][n_heads*128] rows with row stride in_row_stride (views of the fused QKV
+ *            projection output are fine)
+ *   rope: fp32 [s_l][64][2][2] rotation matrices, token row stride rope_row_stride
+ *         (elements); pair i rotates (x[i], x[i+64]):
+ *           out[i] = m00*x[i] + m01*x[i+64],  out[i+64] = m10*x[i] + m11*x[i+64]
+ *         NULL = no rotary embedding (plain RMSNorm)
+ *   q_weight, k_weight: bf16 [128] RMSNorm weights, NULL = unit weight
+ *   y = x * (1 / sqrt(mean(x^2) + eps)) * w, computed in fp32, rounded once to bf16.
+ *   outputs: head h, token j of q (k, v) lands at
+ *     out + (h / heads_per_rank) * out_rank_stride + (h % heads_per_rank) * out_head_stride + j * 128
+ *   v is copied unchanged. */
+int h3_qknorm_rope_pack(const void* q, const void* k, const void* v, int64_t in_row_stride, const float* rope,
+                        int64_t rope_row_stride, const void* q_weight, const void* k_weight, float eps, void* q_out,
+                        void* k_out, void* v_out, int64_t s_l, int64_t n_heads, int64_t heads_per_rank,
+                        int64_t out_rank_stride, int64_t out_head_stride, void* stream);
+
+/* Receive-side reorder of the seq->head all-to-all: the permute copy of
+ * harness/sp_runtime.py:71. recv holds, for each source rank r, n_tensors tensors of
+ * [heads_per_rank][s_l][128]:
+ *   recv + r * recv_rank_stride + t * recv_tensor_stride + h * s_l*128 + j*128
+ * and tensor t lands as [heads_per_rank][world*s_l][128] at out + t * out_tensor_stride. */
+int h3_seq_to_head_unpack(const void* recv, void* out, int64_t world, int64_t heads_per_rank, int64_t s_l,
+                          int64_t n_tensors, int64_t recv_rank_stride, int64_t recv_tensor_stride,
+                          int64_t out_tensor_stride, void* stream);
+
+/* Head-major [n_heads][s_l][128] -> token-major [s_l][n_heads*128]: the
+ * transpose(1, 2).reshape(s, H*D) copy ahead of out_proj (harness/sp_runtime.py:125)
+ * applied to the head->seq all-to-all receive buffer (:76-77). */
+int h3_head_to_seq_unpack(const void* recv, void* out, int64_t n_heads, int64_t s_l, void* stream);
+
+/* Tile known-answer tests of the tcgen05 path (cf. attn_sm80/microtest.py:10-26):
+ *   h3_tile_kat_qk: s_out[128][128] fp32 = q[128][128] . k[128][128]^T
+ *   h3_tile_kat_pv: o_out[128][128] fp32 = p[128][128] . v[128][128]  (p written to TMEM
+ *                   exactly as the softmax warps write P) */
+int h3_tile_kat_qk(const void* q, const void* k, float* s_out, int32_t* status, void* stream);
+int h3_tile_kat_pv(const void* p, const void* v, float* o_out, int32_t* status, void* stream);
+
+/* Synchronise `stream`, then return the status word's value (>= 0), or H3_ERR_CUDA. */
+int h3_status_read(const int32_t* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* H3ATTN_H_ */

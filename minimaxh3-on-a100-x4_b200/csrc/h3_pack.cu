@@ -1,0 +1,223 @@
+// HBM-bound data-movement kernels around the Ulysses all-to-alls:
+//   * qknorm_rope_pack: per-head RMSNorm (+ RoPE) of q and k fused with writing q, k, v
+//     straight into the seq->head send layout (harness/sp_runtime.py:93-104, :69)
+//   * seq_to_head_unpack: receive-side reorder of that exchange (sp_runtime.py:71)
+//   * head_to_seq_unpack: head-major -> token-major rows ahead of out_proj (:125)
+// All traffic is 16-byte vectors; every warp touches whole 128-byte lines.
+#include "h3_ptx.cuh"
+#include "h3attn.h"
+
+namespace h3 {
+namespace pack {
+
+constexpr int kD = 128;
+
+__device__ __forceinline__ void bf16x8_to_f32(const uint4& u, float* f) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+__device__ __forceinline__ uint4 f32_to_bf16x8(const float* f) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) w[i] = pack_bf16x2(f[2 * i], f[2 * i + 1]);
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// One 8-lane group per (token, tensor, head) row of 128 elements. Lane g of the group
+// holds elements [8g, 8g+8) and [64+8g, 64+8g+8), so every rotary pair (i, i+64) is
+// in one thread. Sum of squares: the lane's 16 squares in element order, then an
+// xor-butterfly over the group (distances 4, 2, 1). All products and sums are
+// separately rounded fp32 operations (no contraction) so the CPU restatement in
+// oracle/ reproduces every bit.
+__global__ void __launch_bounds__(256) qknorm_rope_pack_kernel(
+    const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v,
+    long long in_row_stride, const float* __restrict__ rope, long long rope_row_stride,
+    const __nv_bfloat16* __restrict__ qw, const __nv_bfloat16* __restrict__ kw, float eps,
+    __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ k_out, __nv_bfloat16* __restrict__ v_out,
+    long long s_l, int n_heads, int heads_per_rank, long long out_rank_stride, long long out_head_stride) {
+  const long long n_groups = s_l * 3ll * n_heads;
+  const long long gid_raw = (long long)blockIdx.x * (blockDim.x >> 3) + (threadIdx.x >> 3);
+  const bool live = gid_raw < n_groups;
+  const long long gid = live ? gid_raw : n_groups - 1;  // idle lanes still join the shuffles
+  const int g = threadIdx.x & 7;
+  const int h = (int)(gid % n_heads);
+  const long long tt = gid / n_heads;
+  const int tensor = (int)(tt % 3);
+  const long long tok = tt / 3;
+
+  const __nv_bfloat16* src = tensor == 0 ? q : (tensor == 1 ? k : v);
+  __nv_bfloat16* dst = tensor == 0 ? q_out : (tensor == 1 ? k_out : v_out);
+  const __nv_bfloat16* row = src + tok * in_row_stride + (long long)h * kD;
+  __nv_bfloat16* orow = dst + (long long)(h / heads_per_rank) * out_rank_stride +
+                        (long long)(h % heads_per_rank) * out_head_stride + tok * kD;
+
+  const uint4 u0 = __ldg(reinterpret_cast<const uint4*>(row + 8 * g));
+  const uint4 u1 = __ldg(reinterpret_cast<const uint4*>(row + 64 + 8 * g));
+  // v rows run the same (discarded) arithmetic so every lane of the warp reaches the
+  // shuffles below even when a warp mixes tensors (n_heads not a multiple of 4).
+  float x[16];
+  bf16x8_to_f32(u0, x);
+  bf16x8_to_f32(u1, x + 8);
+  float acc = __fmul_rn(x[0], x[0]);
+#pragma unroll
+  for (int i = 1; i < 16; ++i) acc = __fadd_rn(acc, __fmul_rn(x[i], x[i]));
+  // 8-lane butterfly; the group is aligned to 8 lanes so xor stays inside it.
+  const unsigned full = 0xffffffffu;
+  acc = __fadd_rn(acc, __shfl_xor_sync(full, acc, 4));
+  acc = __fadd_rn(acc, __shfl_xor_sync(full, acc, 2));
+  acc = __fadd_rn(acc, __shfl_xor_sync(full, acc, 1));
+  const float mean = __fmul_rn(acc, 0.0078125f);  // / 128, exact
+  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+  const __nv_bfloat16* w = tensor == 0 ? qw : kw;
+  float y[16];
+  if (w != nullptr) {
+    float wf[16];
+    bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(w + 8 * g)), wf);
+    bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(w + 64 + 8 * g)), wf + 8);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) y[i] = __fmul_rn(__fmul_rn(x[i], r), wf[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) y[i] = __fmul_rn(x[i], r);
+  }
+  if (rope != nullptr) {
+    const float4* m = reinterpret_cast<const float4*>(rope + tok * rope_row_stride) + 8 * g;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 mm = __ldg(m + i);  // (m00, m01, m10, m11) of pair 8g+i
+      const float a = y[i], b = y[8 + i];
+      y[i] = __fadd_rn(__fmul_rn(mm.x, a), __fmul_rn(mm.y, b));
+      y[8 + i] = __fadd_rn(__fmul_rn(mm.z, a), __fmul_rn(mm.w, b));
+    }
+  }
+  if (live) {
+    if (tensor == 2) {  // v: copied unchanged into the send layout
+      reinterpret_cast<uint4*>(orow + 8 * g)[0] = u0;
+      reinterpret_cast<uint4*>(orow + 64 + 8 * g)[0] = u1;
+    } else {
+      reinterpret_cast<uint4*>(orow + 8 * g)[0] = f32_to_bf16x8(y);
+      reinterpret_cast<uint4*>(orow + 64 + 8 * g)[0] = f32_to_bf16x8(y + 8);
+    }
+  }
+}
+
+// Chunk (r, t, h) of s_l*128 contiguous elements moves to out_t[h][r*s_l ...]: grid.y
+// enumerates chunks, grid.x strides 16-byte vectors inside a chunk.
+__global__ void __launch_bounds__(256) seq_to_head_unpack_kernel(const uint4* __restrict__ recv,
+                                                                  uint4* __restrict__ out, int world,
+                                                                  int heads_per_rank, long long s_l, int n_tensors,
+                                                                  long long recv_rank_stride,
+                                                                  long long recv_tensor_stride,
+                                                                  long long out_tensor_stride) {
+  const int chunk = blockIdx.y;
+  const int h = chunk % heads_per_rank;
+  const int t = (chunk / heads_per_rank) % n_tensors;
+  const int r = chunk / (heads_per_rank * n_tensors);
+  const long long nvec = s_l * (kD / 8);
+  // strides are in bf16 elements; 8 elements per uint4
+  const uint4* src = recv + (r * recv_rank_stride + t * recv_tensor_stride + (long long)h * s_l * kD) / 8;
+  uint4* dst = out + (t * out_tensor_stride + (long long)h * world * s_l * kD + (long long)r * s_l * kD) / 8;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += (long long)gridDim.x * blockDim.x)
+    dst[i] = __ldg(src + i);
+}
+
+// out[j][h][:] = in[h][j][:] for 256-byte rows: one warp per row pair, 16 B per lane.
+__global__ void __launch_bounds__(256) head_to_seq_unpack_kernel(const uint4* __restrict__ in,
+                                                                  uint4* __restrict__ out, int n_heads,
+                                                                  long long s_l) {
+  const long long rows = (long long)n_heads * s_l;
+  const long long first = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 4;  // 16 lanes per row
+  const int l = threadIdx.x & 15;
+  const long long stride = ((long long)gridDim.x * blockDim.x) >> 4;
+  for (long long rid = first; rid < rows; rid += stride) {
+    const long long j = rid / n_heads;  // output-major walk: consecutive rows write consecutive memory
+    const int h = (int)(rid % n_heads);
+    out[rid * 16 + l] = __ldg(in + ((long long)h * s_l + j) * 16 + l);
+  }
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+static int grid_for(long long work_items, int per_block, int max_blocks) {
+  long long b = (work_items + per_block - 1) / per_block;
+  if (b < 1) b = 1;
+  if (b > max_blocks) b = max_blocks;
+  return (int)b;
+}
+
+}  // namespace pack
+}  // namespace h3
+
+using namespace h3::pack;
+
+extern "C" int h3_version(void) { return H3ATTN_VERSION; }
+
+extern "C" int h3_qknorm_rope_pack(const void* q, const void* k, const void* v, int64_t in_row_stride,
+                                   const float* rope, int64_t rope_row_stride, const void* q_weight,
+                                   const void* k_weight, float eps, void* q_out, void* k_out, void* v_out,
+                                   int64_t s_l, int64_t n_heads, int64_t heads_per_rank, int64_t out_rank_stride,
+                                   int64_t out_head_stride, void* stream) {
+  if (!q || !k || !v || !q_out || !k_out || !v_out) return H3_ERR_NULL;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(q_out) || !aligned16(k_out) ||
+      !aligned16(v_out) || (rope && !aligned16(rope)) || (q_weight && !aligned16(q_weight)) ||
+      (k_weight && !aligned16(k_weight)))
+    return H3_ERR_ALIGN;
+  if (s_l < 1 || n_heads < 1 || heads_per_rank < 1 || n_heads % heads_per_rank) return H3_ERR_SHAPE;
+  if (s_l * 3 * n_heads > (1ll << 40)) return H3_ERR_SHAPE;
+  if (in_row_stride < n_heads * 128 || (in_row_stride % 8) || (out_rank_stride % 8) || (out_head_stride % 8) ||
+      (rope && (rope_row_stride < 256 || (rope_row_stride % 4))))
+    return H3_ERR_STRIDE;
+  if (!(eps >= 0.f)) return H3_ERR_SHAPE;
+  const long long groups = s_l * 3 * n_heads;
+  const long long blocks = (groups + 31) / 32;  // 32 groups of 8 lanes per 256-thread block
+  if (blocks > 0x7fffffffll) return H3_ERR_SHAPE;
+  qknorm_rope_pack_kernel<<<(unsigned)blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const __nv_bfloat16*>(q), reinterpret_cast<const __nv_bfloat16*>(k),
+      reinterpret_cast<const __nv_bfloat16*>(v), in_row_stride, rope, rope_row_stride,
+      reinterpret_cast<const __nv_bfloat16*>(q_weight), reinterpret_cast<const __nv_bfloat16*>(k_weight), eps,
+      reinterpret_cast<__nv_bfloat16*>(q_out), reinterpret_cast<__nv_bfloat16*>(k_out),
+      reinterpret_cast<__nv_bfloat16*>(v_out), s_l, (int)n_heads, (int)heads_per_rank, out_rank_stride,
+      out_head_stride);
+  return cudaGetLastError() == cudaSuccess ? H3_OK : H3_ERR_LAUNCH;
+}
+
+extern "C" int h3_seq_to_head_unpack(const void* recv, void* out, int64_t world, int64_t heads_per_rank,
+                                     int64_t s_l, int64_t n_tensors, int64_t recv_rank_stride,
+                                     int64_t recv_tensor_stride, int64_t out_tensor_stride, void* stream) {
+  if (!recv || !out) return H3_ERR_NULL;
+  if (!aligned16(recv) || !aligned16(out)) return H3_ERR_ALIGN;
+  if (world < 1 || heads_per_rank < 1 || s_l < 1 || n_tensors < 1) return H3_ERR_SHAPE;
+  if (world * heads_per_rank * n_tensors > 65535) return H3_ERR_SHAPE;
+  if ((recv_rank_stride % 8) || (recv_tensor_stride % 8) || (out_tensor_stride % 8)) return H3_ERR_STRIDE;
+  const long long nvec = s_l * 16;
+  dim3 grid((unsigned)grid_for(nvec, 256, 64), (unsigned)(world * heads_per_rank * n_tensors));
+  seq_to_head_unpack_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint4*>(recv), reinterpret_cast<uint4*>(out), (int)world, (int)heads_per_rank, s_l,
+      (int)n_tensors, recv_rank_stride, recv_tensor_stride, out_tensor_stride);
+  return cudaGetLastError() == cudaSuccess ? H3_OK : H3_ERR_LAUNCH;
+}
+
+extern "C" int h3_head_to_seq_unpack(const void* recv, void* out, int64_t n_heads, int64_t s_l, void* stream) {
+  if (!recv || !out) return H3_ERR_NULL;
+  if (!aligned16(recv) || !aligned16(out)) return H3_ERR_ALIGN;
+  if (n_heads < 1 || s_l < 1 || n_heads > 65535) return H3_ERR_SHAPE;
+  const long long rows = n_heads * s_l;
+  head_to_seq_unpack_kernel<<<grid_for(rows * 16, 256, 148 * 16), 256, 0,
+                              reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint4*>(recv), reinterpret_cast<uint4*>(out), (int)n_heads, s_l);
+  return cudaGetLastError() == cudaSuccess ? H3_OK : H3_ERR_LAUNCH;
+}
+
+extern "C" int h3_status_read(const int32_t* status, void* stream) {
+  if (!status) return H3_ERR_NULL;
+  int32_t host = 0;
+  if (cudaMemcpyAsync(&host, status, sizeof(int32_t), cudaMemcpyDeviceToHost,
+                      reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return H3_ERR_CUDA;
+  if (cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess) return H3_ERR_CUDA;
+  return host;
+}

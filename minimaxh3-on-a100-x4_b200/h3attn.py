@@ -1,0 +1,268 @@
+"""Torch-facing binding of libh3attn.so (the sm_100a kernels behind include/h3attn.h).
+
+Every function here validates its tensors, passes raw device pointers, element strides
+and the current CUDA stream through ctypes, and raises on a negative return code. There
+is no CPU path: a missing library or a non-CUDA tensor is an error.
+
+Reference counterparts:
+  attention            SDPA FLASH call, harness/sp_runtime.py:119-121 (and the unwired
+                       fa3(q, k, v, o) of attn_sm80/attn_sm80.py:26-31)
+  qknorm_rope_pack     ck.rms_rope_split_half_ + transposes + send reshape, sp_runtime.py:93-104, :69
+  seq_to_head_unpack   receive-side permute copy, sp_runtime.py:71
+  head_to_seq_unpack   transpose/reshape ahead of out_proj, sp_runtime.py:125
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libh3attn.so")
+D = 128
+
+_ERRORS = {
+    -1: "a required pointer is NULL",
+    -2: "a pointer is not 16-byte aligned",
+    -3: "a size is out of range",
+    -4: "a stride is not a multiple of 8 elements or is too small",
+    -5: "the CUDA runtime refused the launch",
+    -6: "cuTensorMapEncodeTiled rejected the layout",
+    -7: "driver entry point unavailable",
+    -8: "unsupported configuration",
+    -9: "a CUDA runtime call failed",
+}
+STATUS_NAMES = {
+    0: "ok", 1: "timeout waiting for Q tiles", 2: "timeout in the K/V ring", 3: "timeout waiting for S",
+    4: "timeout waiting for P", 5: "timeout waiting for O", 6: "timeout draining copies", 7: "timeout in a tile KAT",
+}
+
+_lib = None
+_status = {}
+
+
+class H3Error(RuntimeError):
+    pass
+
+
+def lib() -> ctypes.CDLL:
+    """Load libh3attn.so once. Raises ImportError when it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: build it with `python {os.path.join(HERE, 'build.py')}`")
+        L = ctypes.CDLL(LIB_PATH)
+        i64, vp, f32, i32p = ctypes.c_int64, ctypes.c_void_p, ctypes.c_float, ctypes.c_void_p
+        L.h3_version.restype = ctypes.c_int
+        L.h3_attn_fwd.argtypes = [vp, vp, vp, vp] + [i64] * 11 + [f32, i32p, vp]
+        L.h3_attn_fwd.restype = ctypes.c_int
+        L.h3_qknorm_rope_pack.argtypes = [vp, vp, vp, i64, vp, i64, vp, vp, f32, vp, vp, vp, i64, i64, i64, i64,
+                                          i64, vp]
+        L.h3_qknorm_rope_pack.restype = ctypes.c_int
+        L.h3_seq_to_head_unpack.argtypes = [vp, vp] + [i64] * 7 + [vp]
+        L.h3_seq_to_head_unpack.restype = ctypes.c_int
+        L.h3_head_to_seq_unpack.argtypes = [vp, vp, i64, i64, vp]
+        L.h3_head_to_seq_unpack.restype = ctypes.c_int
+        L.h3_tile_kat_qk.argtypes = [vp, vp, vp, i32p, vp]
+        L.h3_tile_kat_qk.restype = ctypes.c_int
+        L.h3_tile_kat_pv.argtypes = [vp, vp, vp, i32p, vp]
+        L.h3_tile_kat_pv.restype = ctypes.c_int
+        L.h3_status_read.argtypes = [i32p, vp]
+        L.h3_status_read.restype = ctypes.c_int
+        _lib = L
+    return _lib
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != 0:
+        raise H3Error(f"{what}: {_ERRORS.get(rc, 'error')} (code {rc})")
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _cuda(t: torch.Tensor, name: str, dtype=torch.bfloat16) -> None:
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise H3Error(f"{name} must be a CUDA tensor (this library has no CPU path)")
+    if t.dtype != dtype:
+        raise H3Error(f"{name} must be {dtype}, got {t.dtype}")
+
+
+def status_word(device=None) -> torch.Tensor:
+    """The int32 device status word this process hands to every kernel on `device`."""
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else torch.device(device).index or 0)
+    st = _status.get(dev.index)
+    if st is None:
+        st = torch.zeros(1, dtype=torch.int32, device=dev)
+        _status[dev.index] = st
+    return st
+
+
+def check_status(device=None) -> None:
+    """Synchronise and raise if a kernel on `device` reported a bounded-wait timeout."""
+    st = status_word(device)
+    code = lib().h3_status_read(ctypes.c_void_p(st.data_ptr()), ctypes.c_void_p(_stream()))
+    if code < 0:
+        _check(code, "h3_status_read")
+    if code != 0:
+        st.zero_()
+        raise H3Error(f"device status {code}: {STATUS_NAMES.get(code, 'unknown')}")
+
+
+# ----------------------------------------------------------------------------- attention
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, s_kv: int | None = None,
+              scale: float | None = None, out: torch.Tensor | None = None, layout: str = "head",
+              world: int = 1) -> torch.Tensor:
+    """Exact attention over heads: q [H, Sq, 128], k/v [H, Skv, 128] (bf16, last dim
+    contiguous, any head/row strides that are multiples of 8). Keys/values stop at s_kv
+    (default Skv). Output layout:
+      "head":  [H, Sq, 128]
+      "token": [Sq, H*128] (what out_proj consumes)
+      "send":  [world, H, Sq/world, 128] -- the head->seq all-to-all send buffer
+    """
+    for n, t in (("q", q), ("k", k), ("v", v)):
+        _cuda(t, n)
+        if t.dim() != 3 or t.shape[-1] != D or t.stride(-1) != 1:
+            raise H3Error(f"{n} must be [heads, rows, 128] with a contiguous last dim, got {tuple(t.shape)}")
+    H, sq, _ = q.shape
+    if k.shape[0] != H or v.shape[0] != H or k.shape[1] != v.shape[1]:
+        raise H3Error("q, k, v disagree on heads or key count")
+    if k.stride() != v.stride():
+        raise H3Error("k and v must share strides")
+    skv_alloc = k.shape[1]
+    s_kv = skv_alloc if s_kv is None else int(s_kv)
+    if not 1 <= s_kv <= skv_alloc:
+        raise H3Error(f"s_kv={s_kv} outside [1, {skv_alloc}]")
+    scale = 1.0 / math.sqrt(D) if scale is None else float(scale)
+    if layout == "head":
+        shape, rank_rows, rank_stride, head_stride, row_stride = (H, sq, D), sq, 0, sq * D, D
+    elif layout == "token":
+        shape, rank_rows, rank_stride, head_stride, row_stride = (sq, H * D), sq, 0, D, H * D
+    elif layout == "send":
+        if sq % world:
+            raise H3Error(f"send layout needs rows {sq} divisible by world {world}")
+        sl = sq // world
+        shape, rank_rows, rank_stride, head_stride, row_stride = (world, H, sl, D), sl, H * sl * D, sl * D, D
+    else:
+        raise H3Error(f"unknown layout {layout!r}")
+    if out is None:
+        out = torch.empty(shape, dtype=torch.bfloat16, device=q.device)
+    else:
+        _cuda(out, "out")
+        if tuple(out.shape) != tuple(shape) or not out.is_contiguous():
+            raise H3Error(f"out must be contiguous {shape}, got {tuple(out.shape)}")
+    rc = lib().h3_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), H, sq, s_kv, q.stride(0),
+                           q.stride(1), k.stride(0), k.stride(1), rank_rows, rank_stride, head_stride, row_stride,
+                           scale, status_word(q.device).data_ptr(), _stream())
+    _check(rc, "h3_attn_fwd")
+    return out
+
+
+# ----------------------------------------------------------------------------- pack / unpack
+def qknorm_rope_pack(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, rope: torch.Tensor | None,
+                     q_weight: torch.Tensor | None, k_weight: torch.Tensor | None, eps: float, world: int,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+    """q, k, v: [S_l, H*128] (views of the fused QKV output are fine; rows may be strided).
+    rope: fp32 [S_l, 64, 2, 2] or None. Returns the seq->head send buffer
+    [world, 3, H/world, S_l, 128] with q and k RMS-normalised (+ rotated)."""
+    for n, t in (("q", q), ("k", k), ("v", v)):
+        _cuda(t, n)
+        if t.dim() == 3:
+            t = t.reshape(t.shape[0], -1)
+        if t.dim() != 2 or t.stride(-1) != 1:
+            raise H3Error(f"{n} must be [tokens, heads*128] with a contiguous last dim")
+    q2, k2, v2 = (t.reshape(t.shape[0], -1) if t.dim() == 3 else t for t in (q, k, v))
+    sl, hd = q2.shape
+    if hd % D or k2.shape != q2.shape or v2.shape != q2.shape:
+        raise H3Error("q, k, v must share shape [tokens, heads*128]")
+    if not (q2.stride(0) == k2.stride(0) == v2.stride(0)):
+        raise H3Error("q, k, v must share a row stride")
+    H = hd // D
+    if H % world:
+        raise H3Error(f"heads {H} not divisible by world {world}")
+    hl = H // world
+    rope_ptr, rope_stride = None, 0
+    if rope is not None:
+        _cuda(rope, "rope", torch.float32)
+        if rope.dim() == 5:
+            if rope.shape[0] != 1:
+                raise H3Error("rope batch dim must be 1")
+            rope = rope[0]
+        if tuple(rope.shape[1:]) != (64, 2, 2) or rope.shape[0] != sl or not rope[0].is_contiguous():
+            raise H3Error(f"rope must be [tokens, 64, 2, 2] fp32 (rot_dim 128), got {tuple(rope.shape)}")
+        rope_ptr, rope_stride = rope.data_ptr(), rope.stride(0)
+    wptr = []
+    for n, w in (("q_weight", q_weight), ("k_weight", k_weight)):
+        if w is None:
+            wptr.append(None)
+            continue
+        _cuda(w, n)
+        if tuple(w.shape) != (D,) or not w.is_contiguous():
+            raise H3Error(f"{n} must be contiguous [128] bf16")
+        wptr.append(w.data_ptr())
+    if out is None:
+        out = torch.empty((world, 3, hl, sl, D), dtype=torch.bfloat16, device=q.device)
+    elif tuple(out.shape) != (world, 3, hl, sl, D) or not out.is_contiguous():
+        raise H3Error("out must be contiguous [world, 3, heads/world, tokens, 128]")
+    tstride = hl * sl * D
+    base = out.data_ptr()
+    rc = lib().h3_qknorm_rope_pack(q2.data_ptr(), k2.data_ptr(), v2.data_ptr(), q2.stride(0), rope_ptr, rope_stride,
+                                   wptr[0], wptr[1], float(eps), base, base + 2 * tstride, base + 4 * tstride, sl, H,
+                                   hl, 3 * tstride, sl * D, _stream())
+    _check(rc, "h3_qknorm_rope_pack")
+    return out
+
+
+def seq_to_head_unpack(recv: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """recv [W, T, Hl, Sl, 128] (one block per source rank) -> [T, Hl, W*Sl, 128]."""
+    _cuda(recv, "recv")
+    if recv.dim() != 5 or recv.shape[-1] != D or not recv.is_contiguous():
+        raise H3Error("recv must be contiguous [world, tensors, heads, tokens, 128]")
+    W, T, hl, sl, _ = recv.shape
+    if out is None:
+        out = torch.empty((T, hl, W * sl, D), dtype=torch.bfloat16, device=recv.device)
+    elif tuple(out.shape) != (T, hl, W * sl, D) or not out.is_contiguous():
+        raise H3Error("out has the wrong shape")
+    rc = lib().h3_seq_to_head_unpack(recv.data_ptr(), out.data_ptr(), W, hl, sl, T, T * hl * sl * D, hl * sl * D,
+                                     hl * W * sl * D, _stream())
+    _check(rc, "h3_seq_to_head_unpack")
+    return out
+
+
+def head_to_seq_unpack(recv: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """[H, Sl, 128] head-major -> [Sl, H*128] token-major."""
+    _cuda(recv, "recv")
+    if recv.dim() != 3 or recv.shape[-1] != D or not recv.is_contiguous():
+        raise H3Error("recv must be contiguous [heads, tokens, 128]")
+    H, sl, _ = recv.shape
+    if out is None:
+        out = torch.empty((sl, H * D), dtype=torch.bfloat16, device=recv.device)
+    elif tuple(out.shape) != (sl, H * D) or not out.is_contiguous():
+        raise H3Error("out has the wrong shape")
+    rc = lib().h3_head_to_seq_unpack(recv.data_ptr(), out.data_ptr(), H, sl, _stream())
+    _check(rc, "h3_head_to_seq_unpack")
+    return out
+
+
+# ----------------------------------------------------------------------------- tile KATs
+def tile_kat_qk(q: torch.Tensor, k: torch.Tensor) -> torch.Tensor:
+    _cuda(q, "q")
+    _cuda(k, "k")
+    assert q.shape == (128, 128) and k.shape == (128, 128) and q.is_contiguous() and k.is_contiguous()
+    s = torch.empty((128, 128), dtype=torch.float32, device=q.device)
+    _check(lib().h3_tile_kat_qk(q.data_ptr(), k.data_ptr(), s.data_ptr(), status_word(q.device).data_ptr(),
+                                _stream()), "h3_tile_kat_qk")
+    return s
+
+
+def tile_kat_pv(p: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    _cuda(p, "p")
+    _cuda(v, "v")
+    assert p.shape == (128, 128) and v.shape == (128, 128) and p.is_contiguous() and v.is_contiguous()
+    o = torch.empty((128, 128), dtype=torch.float32, device=p.device)
+    _check(lib().h3_tile_kat_pv(p.data_ptr(), v.data_ptr(), o.data_ptr(), status_word(p.device).data_ptr(),
+                                _stream()), "h3_tile_kat_pv")
+    return o

@@ -1,0 +1,350 @@
+"""B200 drop-in for the reference's Ulysses sequence-parallel runtime (harness/sp_runtime.py).
+
+Same module API and behaviour, B200 data path underneath:
+
+  init()                       process group (NCCL) + device          (ref :60-65)
+  install(module=None)         patch MiniMaxH3Model.run_blocks and     (ref :258-271)
+                               Attention.forward of the host model module
+  a2a_seq_to_head(x, world)    [1, H, Sl, d] -> [1, H/W, S, d]         (ref :67-71)
+  a2a_head_to_seq(x, world, H) [1, H/W, S, d] -> [1, H, Sl, d]         (ref :73-77)
+  get_timing()                 per-category ms of the last run_blocks  (ref :57-58)
+  RANK, WORLD                  module constants from the environment   (ref :16-17)
+  env SP_TIMING=1, SP_OVERLAP=1, SP_PIECES=N                           (ref :32, :133, :265)
+
+What differs, by design:
+  * The attention layer runs on libh3attn.so (sm_100a): one fused kernel does the q/k
+    RMSNorm + RoPE and writes q, k, v straight into the all-to-all send buffer (one
+    exchange for all three), the attention kernel reads the unpacked receive buffer and
+    writes O straight into the head->seq send layout (or, at W=1, token-major for out_proj).
+  * WORLD == 1 runs the same seam with this library's attention instead of falling through
+    to the host model's own loop (ref :222-223), so W-way output is bit-exact against the
+    1-GPU output of the same kernels.
+  * The SLA sparse-attention branch (ref :79-83, :111-118) is not carried: attention is
+    always the exact dense op.
+  * install() takes the host module as an optional argument (default: ComfyUI's
+    comfy.ldm.minimax.model, as in the reference) and uninstall() restores it.
+  * SP_BACKEND selects the process-group backend (default nccl); LOCAL_RANK, when set,
+    picks the device (torchrun); otherwise cuda:0 as in the reference.
+
+There is no CPU path: the kernels live in h3attn (libh3attn.so) and raise if it is absent.
+"""
+from __future__ import annotations
+
+import os
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
+
+RANK = int(os.environ.get("RANK", "0"))
+WORLD = int(os.environ.get("WORLD_SIZE", "1"))
+_INIT = False
+
+# SP attention is scoped to the block loop: run_blocks sets _SP_ACTIVE while the sharded
+# loop runs and the patched attention defers to the host model's own forward otherwise.
+# _SP_REAL_S is the unpadded sequence length: keys/values stop there (pad path).
+_SP_ACTIVE = False
+_SP_REAL_S = None
+_orig_attn_forward = None
+_orig_run_blocks = None
+_MODULE = None
+
+_ops = None  # the kernel library binding (h3attn); resolved on first use
+
+
+def ops():
+    global _ops
+    if _ops is None:
+        import h3attn
+        h3attn.lib()  # fail loudly here if libh3attn.so is missing
+        _ops = h3attn
+    return _ops
+
+
+# ---- optional per-op timing (SP_TIMING=1): CUDA-event category accumulators ----
+_TIMING = os.environ.get("SP_TIMING") == "1"
+_acc = {}
+_last = {}
+
+
+class _tr:
+    def __init__(self, cat):
+        self.cat = cat
+
+    def __enter__(self):
+        if _TIMING:
+            self.s = torch.cuda.Event(enable_timing=True)
+            self.e = torch.cuda.Event(enable_timing=True)
+            self.s.record()
+        return self
+
+    def __exit__(self, *a):
+        if _TIMING:
+            self.e.record()
+            _acc.setdefault(self.cat, []).append((self.s, self.e))
+        return False
+
+
+def _finalize_timing():
+    global _acc
+    if not _TIMING:
+        return
+    torch.cuda.synchronize()
+    _last.clear()
+    for cat, pairs in _acc.items():
+        _last[cat] = sum(s.elapsed_time(e) for s, e in pairs)
+    _acc = {}
+
+
+def get_timing():
+    return dict(_last)
+
+
+def init(timeout_s: float | None = None):
+    """Join the process group (when WORLD > 1) and select this rank's device."""
+    global _INIT
+    if torch.cuda.is_available():
+        local = int(os.environ.get("LOCAL_RANK", "0")) if torch.cuda.device_count() > 1 else 0
+        torch.cuda.set_device(local)
+    if WORLD > 1 and not dist.is_initialized():
+        backend = os.environ.get("SP_BACKEND", "nccl")
+        kw = {"timeout": timedelta(seconds=timeout_s)} if timeout_s else {}
+        dist.init_process_group(backend, rank=RANK, world_size=WORLD, **kw)
+    _INIT = True
+
+
+def _exchange(send: torch.Tensor) -> torch.Tensor:
+    recv = torch.empty_like(send)
+    dist.all_to_all_single(recv, send)
+    return recv
+
+
+def a2a_seq_to_head(x, world):  # [1,H,Sl,d] -> [1,Hl,S,d]
+    _, H, Sl, d = x.shape
+    hl = H // world
+    send = x.reshape(world, 1, hl, Sl, d).contiguous()
+    recv = _exchange(send) if world > 1 else send
+    return ops().seq_to_head_unpack(recv)[0].unsqueeze(0)
+
+
+def a2a_head_to_seq(x, world, H):  # [1,Hl,S,d] -> [1,H,Sl,d]
+    _, hl, S, d = x.shape
+    Sl = S // world
+    send = x[0].view(hl, world, Sl, d).permute(1, 0, 2, 3).contiguous()
+    recv = _exchange(send) if world > 1 else send
+    return recv.reshape(1, H, Sl, d)
+
+
+def _h3sla_schedule(transformer_options):
+    """The reference's SLA hook (sp_runtime.py:79-83). Sparse attention is not carried:
+    this runtime always runs the exact dense op, so there is never a schedule."""
+    return None
+
+
+def _norm_inputs(self, x, rope_freqs):
+    rope = None
+    if rope_freqs is not None:
+        rot = rope_freqs.shape[-3] * 2
+        if rot != self.head_dim:
+            raise NotImplementedError(f"rotary dim {rot} != head_dim {self.head_dim} is not supported")
+        rope = rope_freqs[0] if rope_freqs.dim() == 5 else rope_freqs
+        if rope.dtype != torch.float32:
+            rope = rope.float()
+    qw = getattr(self.q_norm, "weight", None)
+    kw = getattr(self.k_norm, "weight", None)
+    if qw is not None:
+        qw = qw.to(device=x.device, dtype=x.dtype).contiguous()
+    if kw is not None:
+        kw = kw.to(device=x.device, dtype=x.dtype).contiguous()
+    return rope, qw, kw
+
+
+def _sp_attn_forward(self, x, rope_freqs=None, transformer_options={}):
+    if not _SP_ACTIVE:
+        return _orig_attn_forward(self, x, rope_freqs=rope_freqs, transformer_options=transformer_options)
+    O = ops()
+    s = x.shape[0]
+    H, D, W = self.heads, self.head_dim, WORLD
+    with _tr("qkv"):
+        q, k, v = self.qkv_proj(x).split(H * D, dim=-1)
+        rope, qw, kw = _norm_inputs(self, x, rope_freqs)
+        send = O.qknorm_rope_pack(q, k, v, rope, qw, kw, self.q_norm.eps, W)  # [W, 3, H/W, s, D]
+    with _tr("a2a_fwd"):
+        qkvh = O.seq_to_head_unpack(_exchange(send)) if W > 1 else send[0]  # [3, H/W, W*s, D]
+    with _tr("fa2_local"):
+        S_pad = W * s
+        s_kv = _SP_REAL_S if (_SP_REAL_S is not None and _SP_REAL_S < S_pad) else S_pad
+        if W > 1:
+            o_send = O.attention(qkvh[0], qkvh[1], qkvh[2], s_kv=s_kv, layout="send", world=W)
+        else:
+            o = O.attention(qkvh[0], qkvh[1], qkvh[2], s_kv=s_kv, layout="token")
+    with _tr("a2a_inv"):
+        if W > 1:
+            o_recv = _exchange(o_send)  # [W, H/W, s, D] == [H, s, D]
+    with _tr("out_proj"):
+        if W > 1:
+            o = O.head_to_seq_unpack(o_recv.view(H, s, D))
+        return self.out_proj(o)
+
+
+# ---- comm/compute overlap (exact): Q and O exchanged in token pieces on a side stream ----
+_PIECES = int(os.environ.get("SP_PIECES", "4"))
+_comm_stream = None
+
+
+def _piece_bounds(n, p):
+    base, rem = divmod(n, p)
+    out, s = [], 0
+    for i in range(p):
+        ln = base + (1 if i < rem else 0)
+        if ln == 0:
+            continue
+        out.append((s, s + ln))
+        s += ln
+    return out
+
+
+def _sp_attn_forward_overlap(self, x, rope_freqs=None, transformer_options={}):
+    if not _SP_ACTIVE:
+        return _orig_attn_forward(self, x, rope_freqs=rope_freqs, transformer_options=transformer_options)
+    if WORLD == 1:
+        return _sp_attn_forward(self, x, rope_freqs=rope_freqs, transformer_options=transformer_options)
+    global _comm_stream
+    if _comm_stream is None:
+        _comm_stream = torch.cuda.Stream()
+    O = ops()
+    s = x.shape[0]
+    H, D, W = self.heads, self.head_dim, WORLD
+    q, k, v = self.qkv_proj(x).split(H * D, dim=-1)
+    rope, qw, kw = _norm_inputs(self, x, rope_freqs)
+    send = O.qknorm_rope_pack(q, k, v, rope, qw, kw, self.q_norm.eps, W)  # [W, 3, H/W, s, D]
+    kvh = O.seq_to_head_unpack(_exchange(send[:, 1:].contiguous()))  # K, V first (blocking)
+    S_pad = W * s
+    s_kv = _SP_REAL_S if (_SP_REAL_S is not None and _SP_REAL_S < S_pad) else S_pad
+    pieces = _piece_bounds(s, _PIECES)
+    default = torch.cuda.current_stream()
+    _comm_stream.wait_stream(default)
+    o = torch.empty((s, H * D), dtype=x.dtype, device=x.device)
+
+    def q_piece(lo, hi):
+        qh = O.seq_to_head_unpack(_exchange(send[:, 0:1, :, lo:hi].contiguous()))[0]  # [H/W, W*n, D]
+        qh.record_stream(default)
+        return qh
+
+    with torch.cuda.stream(_comm_stream):
+        qh_next = q_piece(*pieces[0])
+    for i, (lo, hi) in enumerate(pieces):
+        default.wait_stream(_comm_stream)
+        qh_p = qh_next
+        if i + 1 < len(pieces):
+            with torch.cuda.stream(_comm_stream):
+                qh_next = q_piece(*pieces[i + 1])
+        o_send = O.attention(qh_p, kvh[0], kvh[1], s_kv=s_kv, layout="send", world=W)
+        with torch.cuda.stream(_comm_stream):
+            _comm_stream.wait_stream(default)
+            o_send.record_stream(_comm_stream)
+            O.head_to_seq_unpack(_exchange(o_send).view(H, hi - lo, D), out=o[lo:hi])
+    default.wait_stream(_comm_stream)
+    return self.out_proj(o)
+
+
+def _shard_segments(segs, lo, hi):
+    out = []
+    for a, b, row in segs:
+        A, B = max(a, lo), min(b, hi)
+        if A < B:
+            out.append((A - lo, B - lo, row))
+    return out
+
+
+def _sp_block_timed(self, x, t_emb, mod_segments, rope_freqs, transformer_options={}):
+    """Timing-instrumented replica of DiTBlock.forward (ref :203-218)."""
+    MM = _MODULE
+    with _tr("norm_mod"):
+        shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = self.adaln_proj(t_emb)
+        h = MM._mod_scale_shift(self.norm1(x), shift_msa, scale_msa, mod_segments)
+    a = self.attn(h, rope_freqs=rope_freqs, transformer_options=transformer_options)
+    with _tr("residual"):
+        x = MM._mod_gate(x, gate_msa, a, mod_segments)
+    with _tr("norm_mod"):
+        h = MM._mod_scale_shift(self.norm2(x), shift_mlp, scale_mlp, mod_segments)
+    with _tr("ffn"):
+        m = self.mlp(h)
+    with _tr("residual"):
+        return MM._mod_gate(x, gate_mlp, m, mod_segments)
+
+
+def _gather_rows(h_loc: torch.Tensor) -> torch.Tensor:
+    out = torch.empty((WORLD * h_loc.shape[0],) + tuple(h_loc.shape[1:]), dtype=h_loc.dtype, device=h_loc.device)
+    if dist.get_backend() == "nccl":
+        dist.all_gather_into_tensor(out, h_loc.contiguous())
+    else:
+        dist.all_gather(list(out.chunk(WORLD, 0)), h_loc.contiguous())
+    return out
+
+
+def _sp_run_blocks(self, h, t_emb, mod_segments, rope_freqs, transformer_options={}):
+    global _SP_ACTIVE, _SP_REAL_S
+    S = h.shape[0]
+    # Exact uneven-S padding: pad rows go at the tail, outside every modulation segment,
+    # and their key positions are excluded inside attention via _SP_REAL_S.
+    S_pad = ((S + WORLD - 1) // WORLD) * WORLD
+    P = S_pad - S
+    if P > 0:
+        h = torch.cat([h, h.new_zeros(P, h.shape[1])], dim=0)
+        if rope_freqs is not None:
+            pad_shape = (rope_freqs.shape[0], P) + tuple(rope_freqs.shape[2:])
+            rope_freqs = torch.cat([rope_freqs, rope_freqs.new_zeros(pad_shape)], dim=1)
+    Sl = S_pad // WORLD
+    lo, hi = RANK * Sl, (RANK + 1) * Sl
+    h_loc = h[lo:hi].contiguous()
+    rope_loc = rope_freqs[:, lo:hi].contiguous() if rope_freqs is not None else None
+    segs_loc = _shard_segments(mod_segments, lo, hi)
+    blkfn = _sp_block_timed if _TIMING else None
+    _SP_ACTIVE = True
+    _SP_REAL_S = S
+    try:
+        for blk in self.blocks:
+            if blkfn is not None:
+                h_loc = blkfn(blk, h_loc, t_emb, segs_loc, rope_loc, transformer_options=transformer_options)
+            else:
+                h_loc = blk(h_loc, t_emb, segs_loc, rope_loc, transformer_options=transformer_options)
+        with _tr("gather"):
+            out = _gather_rows(h_loc) if WORLD > 1 else h_loc
+    finally:
+        _SP_ACTIVE = False
+        _SP_REAL_S = None
+    _finalize_timing()
+    return out[:S] if P > 0 else out
+
+
+def install(module=None):
+    """Patch the host model module (default: ComfyUI's comfy.ldm.minimax.model)."""
+    global _orig_run_blocks, _orig_attn_forward, _MODULE
+    if module is None:
+        import comfy.ldm.minimax.model as module
+    if _MODULE is not None and _MODULE is not module:
+        uninstall()
+    _MODULE = module
+    if _orig_run_blocks is None:
+        _orig_run_blocks = module.MiniMaxH3Model.run_blocks
+    if _orig_attn_forward is None:
+        _orig_attn_forward = module.Attention.forward
+    overlap = os.environ.get("SP_OVERLAP") == "1"
+    module.Attention.forward = _sp_attn_forward_overlap if overlap else _sp_attn_forward
+    module.MiniMaxH3Model.run_blocks = _sp_run_blocks
+    if RANK == 0:
+        mode = f"overlap(P={_PIECES})" if overlap else "blocking"
+        print(f"[sp_runtime] installed (WORLD={WORLD}) - run_blocks + Ulysses attention patched [{mode}]"
+              + (" [SP_TIMING]" if _TIMING else ""), flush=True)
+
+
+def uninstall():
+    """Restore the host module's original run_blocks / Attention.forward."""
+    global _orig_run_blocks, _orig_attn_forward, _MODULE
+    if _MODULE is not None:
+        if _orig_run_blocks is not None:
+            _MODULE.MiniMaxH3Model.run_blocks = _orig_run_blocks
+        if _orig_attn_forward is not None:
+            _MODULE.Attention.forward = _orig_attn_forward
+    _orig_run_blocks = _orig_attn_forward = _MODULE = None
