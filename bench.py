@@ -1,0 +1,339 @@
+"""Benchmark of the B200 Ulysses attention layer (the BASELINE.json headline metric).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--seq S]
+    (N > 1: python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...)
+
+One step = one exact 56x128-head attention layer over S = 42,000 tokens (config 1 at N=1,
+the Ulysses layer of config 2 at N>1): each rank starts from its token shard of the fused
+QKV projection output, runs the fused qk-RMSNorm + RoPE + send pack, the seq->head
+all-to-all (N>1), attention over its 56/N heads and the full sequence, and the head->seq
+all-to-all back to token-major rows (N>1). FLOPs per step = 4*S^2*128*56 (5.058e13).
+
+Printed by rank 0 as ONE JSON line: value = whole-job TFLOP/s from CUDA events (max over
+ranks), e2e = the same through the public API with the step's input copied from pinned
+host memory and its output read back inside the timed region, roofline of the attention
+kernel against MEASURED_PEAKS.json, the CPU baseline (the reference's own SDPA call on
+this host's cores, bounded sample), and SM clocks sampled during the timed region.
+
+--impl reference times the reference's CPU path for this op (torch SDPA FLASH on the host
+cores, harness/sp_runtime.py:119-121) on bounded samples of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "minimaxh3-on-a100-x4_b200")
+sys.path.insert(0, PKG)
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+METRIC = "ms/layer & TFLOP/s, 56x128 attn S=42k bf16, 1/2/4/8 B200; % dense bf16 peak"
+UNIT = "TFLOP/s"
+HEADS, D = 56, 128
+
+
+def flops_layer(s: int, heads: int = HEADS) -> float:
+    return 4.0 * s * s * D * heads
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return j.get("bf16_tflops"), j.get("bf16_tflops_sustained"), j.get("hbm_gbs"), "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+def profiled_traffic(name: str, seq: int, heads: int):
+    """DRAM bytes (read + write) of one attention launch at `seq` x `heads`, scaled from the
+    ncu capture summarised in profiles/<name> ('capture_seq:' and 'dram_bytes_per_launch:'
+    lines, 56 heads). Q, K, V are read once and O written once, so traffic is linear in
+    S and in the head count. None when no capture has been summarised."""
+    p = os.path.join(ROOT, "profiles", name)
+    if not os.path.exists(p):
+        return None
+    vals = {}
+    with open(p) as f:
+        for line in f:
+            for key in ("capture_seq:", "dram_bytes_per_launch:"):
+                if line.startswith(key):
+                    vals[key] = float(line.split(":", 1)[1].strip())
+    if len(vals) != 2:
+        return None
+    return int(vals["dram_bytes_per_launch:"] * seq / vals["capture_seq:"] * heads / HEADS)
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, n_gpus: int):
+        self.n = n_gpus
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_bench_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.f.close()
+        return False
+
+    def summary(self):
+        if self.proc is None or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                c = [x.strip() for x in line.split(",")]
+                if len(c) < 9 or not c[0].isdigit() or int(c[0]) >= self.n:
+                    continue
+                try:
+                    sm.append(float(c[1]))
+                    mx.append(float(c[2]))
+                except ValueError:
+                    continue
+                for nm, val in zip(names, c[5:9]):
+                    if val.lower() == "active":
+                        reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_sdpa_sample(s_kv: int, heads: int, rows: int, reps: int, threads: int):
+    """The reference's attention call (SDPA FLASH, sp_runtime.py:119-121) in fp32 on the host
+    cores for `heads` heads x `rows` query rows against all s_kv keys. Returns the per-rep times."""
+    from oracle import sdpa_ref
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    q = torch.randn(1, heads, rows, D, generator=g)
+    k = torch.randn(1, heads, s_kv, D, generator=g)
+    v = torch.randn(1, heads, s_kv, D, generator=g)
+    sdpa_ref.attention(q[:, :, :64], k[:, :, :256], v[:, :, :256])  # warm-up
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        sdpa_ref.attention(q, k, v)
+        times.append(time.perf_counter() - t0)
+    return times
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    heads, rows = 1, 4096  # one bounded sample per step: 1 head x 4096 query rows x all keys
+    torch.set_num_threads(threads)
+    times = cpu_sdpa_sample(args.seq, heads, rows, args.warmup + args.steps, threads)[args.warmup:]
+    per = statistics.median(times)
+    fl = 4.0 * rows * args.seq * D * heads
+    val = fl / per / 1e12
+    sample = f"{heads} head x {rows} query rows x {args.seq} keys fp32 per step ({fl:.3g} FLOP)"
+    line = {
+        "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+        "config": config(args),
+        "cpu_baseline": {"value": val, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": sample + "; torch SDPA FLASH on CPU, the reference's attention call"},
+        "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config(args):
+    return {"workload": "ulysses attention layer: qk-RMSNorm+RoPE pack, seq->head all-to-all, exact attention, "
+                        "head->seq all-to-all", "heads": HEADS, "head_dim": D, "seq_len": args.seq, "batch": 1,
+            "parallelism": f"ulysses{args.gpus}",
+            "l2": f"inputs larger than L2: {args.seq * 3 * HEADS * D * 2 / 1e9:.2f} GB of QKV per step"}
+
+
+def run_ours(args, rank: int, world: int, local: int) -> None:
+    import h3attn
+    import h3_model
+
+    dev = torch.device("cuda", local)
+    S, H, W = args.seq, HEADS, world
+    if S % W or H % W:
+        raise SystemExit(f"seq {S} and heads {H} must divide by {W}")
+    sl, hl = S // W, H // W
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    qkv = torch.randn((sl, 3 * H * D), generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    rope = h3_model.rope_freqs_1d(sl, pos0=rank * sl, device=dev)[0].contiguous()
+    ones = torch.ones(D, dtype=torch.bfloat16, device=dev)
+    eps = 1e-6
+    ev_att = []
+
+    def layer(x, out=None, timed=False):
+        q, k, v = x.split(H * D, dim=-1)
+        send = h3attn.qknorm_rope_pack(q, k, v, rope, ones, ones, eps, W)
+        if W > 1:
+            recv = torch.empty_like(send)
+            dist.all_to_all_single(recv, send)
+            qkvh = h3attn.seq_to_head_unpack(recv)
+        else:
+            qkvh = send[0]
+        if timed:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+        if W > 1:
+            o_send = h3attn.attention(qkvh[0], qkvh[1], qkvh[2], layout="send", world=W)
+        else:
+            o = h3attn.attention(qkvh[0], qkvh[1], qkvh[2], layout="token", out=out)
+        if timed:
+            e1.record()
+            ev_att.append((e0, e1))
+        if W > 1:
+            o_recv = torch.empty_like(o_send)
+            dist.all_to_all_single(o_recv, o_send)
+            o = h3attn.head_to_seq_unpack(o_recv.view(H, sl, D), out=out)
+        return o
+
+    def sync_all():
+        torch.cuda.synchronize()
+        if W > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if W == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    # correctness guard: the status word must stay clean
+    for _ in range(args.warmup):
+        layer(qkv)
+    h3attn.check_status()
+    sync_all()
+
+    # ---- device-timed region
+    ev_att.clear()
+    sampler = ClockSampler(W) if rank == 0 else None
+    if sampler:
+        sampler.__enter__()
+    sync_all()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        layer(qkv, timed=True)
+    t1.record()
+    sync_all()
+    if sampler:
+        sampler.__exit__()
+    ms = max_over_ranks(t0.elapsed_time(t1) / args.steps)
+    att_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in ev_att))
+    h3attn.check_status()
+
+    # ---- end-to-end through the public API: pinned host input -> device -> layer -> host
+    host_in = torch.empty(qkv.shape, dtype=qkv.dtype, pin_memory=True)
+    host_in.copy_(qkv)
+    host_out = torch.empty((sl, H * D), dtype=torch.bfloat16, pin_memory=True)
+    dev_in = torch.empty_like(qkv)
+    e2e_steps = max(3, min(args.steps, 10))
+    layer(dev_in.copy_(host_in, non_blocking=True))
+    sync_all()
+    t0.record()
+    for _ in range(e2e_steps):
+        dev_in.copy_(host_in, non_blocking=True)
+        o = layer(dev_in)
+        host_out.copy_(o, non_blocking=True)
+    t1.record()
+    sync_all()
+    e2e_ms = max_over_ranks(t0.elapsed_time(t1) / e2e_steps)
+
+    if rank != 0:
+        return
+    fl = flops_layer(S)
+    burst, sustained, hbm, kind = peaks()
+    att_fl = 4.0 * S * S * D * hl  # one rank's launch
+    achieved = att_fl / (att_ms * 1e-3) / 1e12
+    traffic = profiled_traffic("attn_fwd_s8192_h56_full.md", S, hl)
+    launches = (2 if W == 1 else 4) * args.steps
+    line = {
+        "metric": METRIC, "value": fl / (ms * 1e-3) / 1e12, "unit": UNIT, "n_gpus": W, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config(args),
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": sustained, "unit": "TFLOP/s",
+                     "frac": achieved / sustained, "peak_kind": f"{kind} sustained bf16 (cuBLAS 8192^3 loop)",
+                     "frac_of_burst_peak": achieved / burst, "traffic": traffic, "kernel": "attn_fwd_kernel",
+                     "kernel_ms": att_ms, "flop_per_launch": att_fl},
+        "e2e": {"value": fl / (e2e_ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": qkv.numel() * 2 * W, "d2h_bytes_per_step": sl * H * D * 2 * W},
+        "gpu_launches": launches,
+        "clocks": sampler.summary() if sampler else None,
+    }
+    if W == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        heads, rows = 4, 4096
+        times = cpu_sdpa_sample(S, heads, rows, 5, threads)
+        per = statistics.median(times)
+        cfl = 4.0 * rows * S * D * heads
+        line["cpu_baseline"] = {"value": cfl / per / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
+                                "sample": f"{heads} heads x {rows} query rows x {S} keys fp32 ({cfl:.3g} FLOP), "
+                                          f"median of 5; torch SDPA FLASH on CPU (the reference's attention call)"}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--seq", type=int, default=42000)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    try:
+        run_ours(args, rank, world, local)
+    finally:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,91 @@
+"""The C ABI (include/h3attn.h) on CPU: the library loads, exports every declared entry
+point, and rejects bad arguments before any CUDA work. No kernel runs here."""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "h3attn.h")
+
+
+def declared():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"^\s*int\s+(h3_\w+)\s*\(", src, flags=re.M)))
+
+
+@pytest.fixture(scope="module")
+def L():
+    import h3attn
+    if not os.path.exists(h3attn.LIB_PATH):
+        from build import build
+        build()
+    return h3attn.lib()
+
+
+def test_header_declares_entry_points():
+    names = declared()
+    for n in ("h3_attn_fwd", "h3_qknorm_rope_pack", "h3_seq_to_head_unpack", "h3_head_to_seq_unpack",
+              "h3_status_read", "h3_version", "h3_tile_kat_qk", "h3_tile_kat_pv"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(L):
+    for n in declared():
+        assert hasattr(L, n), n
+
+
+def test_version(L):
+    assert L.h3_version() == 1
+
+
+def test_attn_rejects_bad_arguments_before_launch(L):
+    args = lambda q: [q, q, q, q, 2, 128, 128, 128 * 128, 128, 128 * 128, 128, 128, 0, 128 * 128, 128,
+                      ctypes.c_float(0.088), ctypes.c_void_p(0x1000), None]
+    assert L.h3_attn_fwd(*args(None)) == -1                      # NULL
+    assert L.h3_attn_fwd(*args(ctypes.c_void_p(0x1008))) == -2   # not 16-byte aligned
+    a = args(ctypes.c_void_p(0x1000))
+    a[5] = 0                                                     # s_q = 0
+    assert L.h3_attn_fwd(*a) == -3
+    a = args(ctypes.c_void_p(0x1000))
+    a[8] = 100                                                   # row stride not a multiple of 8
+    assert L.h3_attn_fwd(*a) == -4
+    a = args(ctypes.c_void_p(0x1000))
+    a[15] = ctypes.c_float(-1.0)                                 # scale must be positive
+    assert L.h3_attn_fwd(*a) == -3
+
+
+def test_pack_rejects_bad_arguments_before_launch(L):
+    p = ctypes.c_void_p(0x1000)
+    ok = [p, p, p, 3 * 4 * 128, None, 0, None, None, ctypes.c_float(1e-6), p, p, p, 10, 4, 2, 4 * 10 * 128,
+          10 * 128, None]
+    bad = list(ok)
+    bad[0] = None
+    assert L.h3_qknorm_rope_pack(*bad) == -1
+    bad = list(ok)
+    bad[14] = 3  # heads not divisible into ranks
+    assert L.h3_qknorm_rope_pack(*bad) == -3
+    bad = list(ok)
+    bad[3] = 4 * 128 - 8  # row stride smaller than a row
+    assert L.h3_qknorm_rope_pack(*bad) == -4
+
+
+def test_unpack_rejects_bad_arguments_before_launch(L):
+    p = ctypes.c_void_p(0x1000)
+    assert L.h3_seq_to_head_unpack(None, p, 2, 2, 8, 3, 0, 0, 0, None) == -1
+    assert L.h3_seq_to_head_unpack(p, p, 0, 2, 8, 3, 0, 0, 0, None) == -3
+    assert L.h3_head_to_seq_unpack(p, ctypes.c_void_p(0x1004), 4, 8, None) == -2
+    assert L.h3_status_read(None, None) == -1
+
+
+def test_no_cpu_path():
+    """The binding refuses host tensors instead of computing on the CPU."""
+    import torch
+    import h3attn
+    q = torch.zeros(1, 128, 128, dtype=torch.bfloat16)
+    with pytest.raises(h3attn.H3Error):
+        h3attn.attention(q, q, q)
+    with pytest.raises(h3attn.H3Error):
+        h3attn.qknorm_rope_pack(q[0], q[0], q[0], None, None, None, 1e-6, 1)
