@@ -69,6 +69,33 @@ int h3_attn_fwd(const void* q, const void* k, const void* v, void* o, int64_t n_
                 int64_t o_rank_rows, int64_t o_rank_stride, int64_t o_head_stride, int64_t o_row_stride,
                 float softmax_scale, int32_t* status, void* stream);
 
+/* h3_attn_fwd with an explicit kernel schedule (a tuning hook; h3_attn_fwd uses the
+ * default). All variants compute the same attention within the same tolerance:
+ *   0  two softmax warpgroups run freely, exp2 on MUFU
+ *   1  softmax warpgroups alternate their exp phase (ping-pong token), exp2 on MUFU
+ *   2  ping-pong, every 4th element's exp2 on the FMA pipe (degree-3 minimax polynomial)
+ *   3  ping-pong, every 8th element on the FMA pipe
+ *   4  ping-pong, every 2nd element on the FMA pipe
+ * Returns H3_ERR_UNSUPPORTED for any other value. */
+int h3_attn_fwd_variant(const void* q, const void* k, const void* v, void* o, int64_t n_heads, int64_t s_q,
+                        int64_t s_kv, int64_t q_head_stride, int64_t q_row_stride, int64_t kv_head_stride,
+                        int64_t kv_row_stride, int64_t o_rank_rows, int64_t o_rank_stride, int64_t o_head_stride,
+                        int64_t o_row_stride, float softmax_scale, int32_t* status, int32_t variant, void* stream);
+
+/* Phase profiler (diagnostics; cf. the clock64 phase counters of the reference kernel,
+ * attn_sm80/fa3_sm80_h3.cu:96-105, :572-582): runs variant 0-3 and records clock64()
+ * stamps of CTA (0, 0) for the first trace_iters KV iterations into the device buffer
+ *   trace[((role * trace_iters) + j) * 8 + point]   (int64, 3 * trace_iters * 8 entries)
+ * role 0/1 = softmax warpgroup of Q tile 0/1: points 0 before the S wait, 1 S ready,
+ *   2 S in registers, 3 row max done, 4 exp phase may start, 5 exps done, 6 P handed over;
+ * role 2 = MMA thread: 0 iteration start, 1 P_0 ready, 2 P_0*V issued, 3 next K ready,
+ *   4 next S_0 issued, 5 P_1 ready, 6 iteration issued. */
+int h3_attn_fwd_profile(const void* q, const void* k, const void* v, void* o, int64_t n_heads, int64_t s_q,
+                        int64_t s_kv, int64_t q_head_stride, int64_t q_row_stride, int64_t kv_head_stride,
+                        int64_t kv_row_stride, int64_t o_rank_rows, int64_t o_rank_stride, int64_t o_head_stride,
+                        int64_t o_row_stride, float softmax_scale, int32_t* status, int32_t variant,
+                        long long* trace, int64_t trace_iters, void* stream);
+
 /* Fused per-head qk-RMSNorm + RoPE + seq->head send-buffer pack for one token shard.
  * Replaces comfy_kitchen's in-place rms_rope_split_half_ call (harness/sp_runtime.py:93-99,
  * or q_norm/k_norm when rope is absent, :100-101), the head transposes (:102) and the

@@ -39,11 +39,14 @@ enum Bar : int {
   kBarQFull = 0,
   kBarKVFull = 1,
   kBarKVEmpty = kBarKVFull + kStages,
-  kBarSFull = kBarKVEmpty + kStages,
-  kBarPFull = kBarSFull + 2,
-  kBarODone = kBarPFull + 2,
+  kBarSFull = kBarKVEmpty + kStages,  // S_t ready (per Q tile)
+  kBarPFullA = kBarSFull + 2,         // first 64 keys of P_t in TMEM
+  kBarPFullB = kBarPFullA + 2,        // last 64 keys of P_t in TMEM
+  kBarODoneA = kBarPFullB + 2,        // P_t,first-half * V retired
+  kBarODone = kBarODoneA + 2,         // P_t * V retired
   kBarDrain = kBarODone + 2,
-  kNumBars = kBarDrain + 1
+  kBarTok = kBarDrain + 1,  // softmax ping-pong token, one per warpgroup
+  kNumBars = kBarTok + 2
 };
 
 constexpr uint32_t kOffQ = 0;
@@ -67,28 +70,73 @@ struct Params {
   long long o_head_stride;
   long long o_row_stride;
   int* status;
+  long long* prof;  // phase timestamps of CTA (0, 0) when profiling, else nullptr
+  int prof_iters;
 };
 
-// S = Q K^T for one 128x128 tile pair; both operands K-major, SW128, two 64-column blocks.
-__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t a_base, uint32_t b_base) {
-  constexpr uint32_t idesc = idesc_bf16_f32(128, 128, 0, 0);
-#pragma unroll
-  for (int kk = 0; kk < kD / 16; ++kk) {
-    const uint32_t off = uint32_t(kk >> 2) * kHalfBytes + uint32_t(kk & 3) * 32u;
-    mma_ss(d_tmem, smem_desc_sw128(a_base + off, 16, 1024), smem_desc_sw128(b_base + off, 16, 1024), idesc,
-           kk > 0 ? 1u : 0u);
-  }
+// Phase profiler (the counterpart of the reference kernel's clock64 counters): the first
+// thread of softmax warps 4 and 8 and the MMA thread of CTA (0, 0) record clock64() at
+// fixed points of each KV iteration j < prof_iters into
+//   prof[((role * prof_iters) + j) * 8 + point],  role 0/1 = softmax tile 0/1, role 2 = MMA.
+template <bool kProf>
+__device__ __forceinline__ void prof_mark(const Params& p, bool rec, int role, int j, int point) {
+  if (kProf && rec && j < p.prof_iters) p.prof[((long long)role * p.prof_iters + j) * 8 + point] = clock64();
 }
 
-// O (+)= P V for one tile: P from TMEM (K = keys along columns, two bf16 per column),
-// V MN-major in shared memory (d contiguous), two 64-wide d blocks 16 KB apart.
-__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_base, bool accumulate) {
+// Every 8-MMA group below is ONE asm block with the smem descriptors formed by immediate
+// adds on the low word: the single MMA-issuing thread shares its SM sub-partition with two
+// busy softmax warps, and the tensor pipe queue is shallow, so the instructions it spends
+// per MMA directly become tensor-core idle time. Start addresses stay below 256 KB, so the
+// low-word adds never carry out of the 14-bit start-address field.
+
+// S = Q K^T for one 128x128 tile pair: both operands K-major, SW128, two 64-column blocks
+// 16 KB apart; K steps of 16 elements advance 32 B inside a block.
+__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t a_base, uint32_t b_base) {
+  constexpr uint32_t idesc = idesc_bf16_f32(128, 128, 0, 0);
+  const uint64_t ad = smem_desc_sw128(a_base, 16, 1024), bd = smem_desc_sw128(b_base, 16, 1024);
+  const uint32_t alo = uint32_t(ad), ahi = uint32_t(ad >> 32), blo = uint32_t(bd), bhi = uint32_t(bd >> 32);
+#define H3_QK_STEP(OFF) \
+  "add.u32 la, %1, " #OFF ";\n\t add.u32 lb, %3, " #OFF ";\n\t" \
+  "mov.b64 da, {la, %2};\n\t mov.b64 db, {lb, %4};\n\t" \
+  "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %5, pt;\n\t"
+  asm volatile(
+      "{\n\t.reg .pred pf, pt;\n\t.reg .b32 la, lb;\n\t.reg .b64 da, db;\n\t"
+      "setp.ne.b32 pf, %0, %0;\n\t setp.eq.b32 pt, %0, %0;\n\t"
+      "mov.b64 da, {%1, %2};\n\t mov.b64 db, {%3, %4};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %5, pf;\n\t"
+      H3_QK_STEP(2) H3_QK_STEP(4) H3_QK_STEP(6) H3_QK_STEP(1024) H3_QK_STEP(1026) H3_QK_STEP(1028) H3_QK_STEP(1030)
+      "}\n" ::"r"(d_tmem), "r"(alo), "r"(ahi), "r"(blo), "r"(bhi), "r"(idesc)
+      : "memory");
+#undef H3_QK_STEP
+}
+
+// O (+)= P V over 64 keys (half = 0: keys 0..63, half = 1: keys 64..127) of one tile: P
+// from TMEM (keys along columns, two bf16 per 32-bit column, 8 columns per K step), V
+// MN-major in shared memory (d contiguous), two 64-wide d blocks 16 KB apart (LBO), 8-key
+// groups 1 KB apart (SBO); K steps advance 2 KB. `accumulate` applies to the first step.
+__device__ __forceinline__ void issue_pv_half(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_base, int half,
+                                              bool accumulate) {
   constexpr uint32_t idesc = idesc_bf16_f32(128, 128, 0, 1);
-#pragma unroll
-  for (int kk = 0; kk < kBlockN / 16; ++kk) {
-    mma_ts(d_tmem, p_tmem + uint32_t(kk) * 8u, smem_desc_sw128(v_base + uint32_t(kk) * 2048u, kHalfBytes, 1024),
-           idesc, (accumulate || kk > 0) ? 1u : 0u);
-  }
+  const uint64_t bd = smem_desc_sw128(v_base + uint32_t(half) * 4u * 2048u, kHalfBytes, 1024);
+  const uint32_t blo = uint32_t(bd), bhi = uint32_t(bd >> 32);
+  const uint32_t pa = p_tmem + uint32_t(half) * 32u;
+#define H3_PV_STEP(KK) \
+  "add.u32 ta, %1, " #KK "*8;\n\t add.u32 lb, %2, " #KK "*128;\n\t mov.b64 db, {lb, %3};\n\t" \
+  "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], db, %4, pt;\n\t"
+  asm volatile(
+      "{\n\t.reg .pred pf, pt;\n\t.reg .b32 ta, lb;\n\t.reg .b64 db;\n\t"
+      "setp.ne.b32 pf, %5, 0;\n\t setp.eq.b32 pt, %5, %5;\n\t"
+      "mov.b64 db, {%2, %3};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %4, pf;\n\t"
+      H3_PV_STEP(1) H3_PV_STEP(2) H3_PV_STEP(3)
+      "}\n" ::"r"(d_tmem), "r"(pa), "r"(blo), "r"(bhi), "r"(idesc), "r"(accumulate ? 1u : 0u)
+      : "memory");
+#undef H3_PV_STEP
+}
+
+__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_base, bool accumulate) {
+  issue_pv_half(d_tmem, p_tmem, v_base, 0, accumulate);
+  issue_pv_half(d_tmem, p_tmem, v_base, 1, true);
 }
 
 // Bounded wait that ignores the abort flag: used while draining copies/MMAs before exit.
@@ -102,6 +150,36 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, int* s
   }
 }
 
+// 2^x on the FMA pipe (relieves MUFU): n = round(x) through the 1.5*2^23 shifter,
+// f = x - n in [-1/2, 1/2], 2^f by a degree-3 polynomial with minimax relative error
+// 7.5e-5 (Remez fit, csrc/gen_exp2_poly.py), n added straight into the exponent field.
+// x < -125 returns 0 (masked keys stay exactly zero; results stay normal numbers). The operation order is fixed,
+// so results do not depend on launch shape.
+__device__ __forceinline__ float ex2_poly(float x) {
+  const float shifter = 12582912.0f;  // 1.5 * 2^23
+  const float xc = fmaxf(x, -125.0f);
+  const float t = __fadd_rn(xc, shifter);
+  const float n = __fsub_rn(t, shifter);
+  const float f = __fsub_rn(xc, n);
+  float q = __fmaf_rn(5.517166853e-02f, f, 2.426111251e-01f);
+  q = __fmaf_rn(q, f, 6.932609677e-01f);
+  q = __fmaf_rn(q, f, 9.999280572e-01f);
+  const int ni = __float_as_int(t) - 0x4B400000;
+  const float r = __int_as_float(__float_as_int(q) + (ni << 23));
+  return x < -125.0f ? 0.0f : r;
+}
+
+// Element idx of a row takes the FMA-pipe exp2 when kEmu > 0 and idx % kEmu == kEmu - 1.
+template <int kEmu>
+__device__ __forceinline__ float ex2_mixed(float x, int idx) {
+  if (kEmu > 0 && (idx % (kEmu > 0 ? kEmu : 1)) == kEmu - 1) return ex2_poly(x);
+  return ex2_approx(x);
+}
+
+// kPingPong: the two softmax warpgroups take turns (a token passed through two mbarriers)
+// for their exp phase, so one exponentiates while the tensor core runs the other's
+// P*V and next Q*K^T, instead of both contending for MUFU at once.
+template <bool kPingPong, int kEmu, bool kProf>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                     const __grid_constant__ CUtensorMap tmap_v, const Params p) {
@@ -127,8 +205,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(bar(kBarSFull + t), 1);
-      mbar_init(bar(kBarPFull + t), 128);
+      mbar_init(bar(kBarPFullA + t), 128);
+      mbar_init(bar(kBarPFullB + t), 128);
+      mbar_init(bar(kBarODoneA + t), 1);
       mbar_init(bar(kBarODone + t), 1);
+      mbar_init(bar(kBarTok + t), 128);
     }
     mbar_init(bar(kBarDrain), 1);
     *abort_flag = (*reinterpret_cast<volatile int*>(p.status) != 0) ? 1 : 0;
@@ -186,53 +267,54 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
+    // Ring order is K_0, V_0, K_1, V_1, ...; iteration j holds V_j and K_{j+1}. Both are
+    // waited for before any P of iteration j, so no barrier wait sits between P_t * V_j
+    // and the next S_t = Q_t K_{j+1}^T.
     if (lane == 0 && !grid_aborted) {
       const uint32_t sq = sbase + kOffQ;
       const uint32_t skv = sbase + kOffKV;
-      int it = 0;
+      const bool rec = blockIdx.x == 0 && blockIdx.y == 0;
       auto wait_full = [&](int st_it) -> bool {
-        const int st = st_it % kStages;
-        return mbar_wait(bar(kBarKVFull + st), uint32_t(st_it / kStages) & 1u, ctx, kStatusTimeoutKV);
+        return mbar_wait(bar(kBarKVFull + st_it % kStages), uint32_t(st_it / kStages) & 1u, ctx, kStatusTimeoutKV);
       };
-      bool ok = mbar_wait(bar(kBarQFull), 0, ctx, kStatusTimeoutQ);
-      if (ok) ok = wait_full(it);
+      bool ok = mbar_wait(bar(kBarQFull), 0, ctx, kStatusTimeoutQ) && wait_full(0);
       if (ok) {
         tc_fence_after();
-        const int st = it % kStages;
-        issue_qk(tmem + col_s(0), sq, skv + st * kTileBytes);
+        issue_qk(tmem + col_s(0), sq, skv);
         mma_commit(bar(kBarSFull + 0));
-        issue_qk(tmem + col_s(1), sq + kTileBytes, skv + st * kTileBytes);
+        issue_qk(tmem + col_s(1), sq + kTileBytes, skv);
         mma_commit(bar(kBarSFull + 1));
-        mma_commit(bar(kBarKVEmpty + st));
-        ++it;
+        mma_commit(bar(kBarKVEmpty + 0));
       }
       for (int j = 0; ok && j < n_kv; ++j) {
-        const int it_v = it++;
+        prof_mark<kProf>(p, rec, 2, j, 0);
+        const int it_v = 2 * j + 1, it_k = 2 * j + 2;
+        const bool next = j + 1 < n_kv;
         if (!(ok = wait_full(it_v))) break;
-        const int stv = it_v % kStages;
+        if (next && !(ok = wait_full(it_k))) break;
+        tc_fence_after();
+        const uint32_t sv = skv + (it_v % kStages) * kTileBytes;
+        const uint32_t sk = skv + (it_k % kStages) * kTileBytes;
         const uint32_t ph = uint32_t(j) & 1u;
-        if (!(ok = mbar_wait(bar(kBarPFull + 0), ph, ctx, kStatusTimeoutP))) break;
-        tc_fence_after();
-        issue_pv(tmem + col_o(0), tmem + col_p(0), skv + stv * kTileBytes, j > 0);
-        mma_commit(bar(kBarODone + 0));
-        int stk = -1;
-        if (j + 1 < n_kv) {
-          const int it_k = it++;
-          if (!(ok = wait_full(it_k))) break;
+        prof_mark<kProf>(p, rec, 2, j, 1);
+        for (int t = 0; t < 2; ++t) {
+          if (!(ok = mbar_wait(bar(kBarPFullA + t), ph, ctx, kStatusTimeoutP))) break;
+          prof_mark<kProf>(p, rec, 2, j, 2 + 3 * t);
           tc_fence_after();
-          stk = it_k % kStages;
-          issue_qk(tmem + col_s(0), sq, skv + stk * kTileBytes);
-          mma_commit(bar(kBarSFull + 0));
-        }
-        if (!(ok = mbar_wait(bar(kBarPFull + 1), ph, ctx, kStatusTimeoutP))) break;
-        tc_fence_after();
-        issue_pv(tmem + col_o(1), tmem + col_p(1), skv + stv * kTileBytes, j > 0);
-        mma_commit(bar(kBarODone + 1));
-        mma_commit(bar(kBarKVEmpty + stv));
-        if (stk >= 0) {
-          issue_qk(tmem + col_s(1), sq + kTileBytes, skv + stk * kTileBytes);
-          mma_commit(bar(kBarSFull + 1));
-          mma_commit(bar(kBarKVEmpty + stk));
+          issue_pv_half(tmem + col_o(t), tmem + col_p(t), sv, 0, j > 0);
+          mma_commit(bar(kBarODoneA + t));
+          if (!(ok = mbar_wait(bar(kBarPFullB + t), ph, ctx, kStatusTimeoutP))) break;
+          prof_mark<kProf>(p, rec, 2, j, 3 + 3 * t);
+          tc_fence_after();
+          issue_pv_half(tmem + col_o(t), tmem + col_p(t), sv, 1, true);
+          mma_commit(bar(kBarODone + t));
+          if (t == 1) mma_commit(bar(kBarKVEmpty + it_v % kStages));
+          if (next) {
+            issue_qk(tmem + col_s(t), sq + t * kTileBytes, sk);
+            mma_commit(bar(kBarSFull + t));
+            if (t == 1) mma_commit(bar(kBarKVEmpty + it_k % kStages));
+          }
+          prof_mark<kProf>(p, rec, 2, j, 4 + 3 * t);
         }
       }
       // Every issued MMA must retire before TMEM is released.
@@ -241,6 +323,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ softmax + epilogue
+    // The 128 keys of a tile are handled as two 64-key halves: each half has its own row
+    // max / rescale step and its own P hand-off, so P_a * V runs on the tensor core while
+    // the second half's exponentials are computed. Online softmax across halves is exact.
     const int t = (warp - 4) >> 2;  // Q tile
     const int quad = warp & 3;      // TMEM lane quadrant this warp may access
     const uint32_t lane_off = uint32_t(quad * 32) << 16;
@@ -252,9 +337,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m_run = -INFINITY;
     float l_run = 0.f;
     bool ok = !grid_aborted;
+    const bool rec = blockIdx.x == 0 && blockIdx.y == 0 && quad == 0 && lane == 0;
+
+    // Rescale O (and l) of the rows whose running max grew by more than 2^8; `o_ready`
+    // says whether every P*V accumulated so far has retired.
+    auto rescale = [&](float m_new, uint32_t o_bar, uint32_t o_parity, bool o_ready) -> bool {
+      const bool need = m_new > m_run + kRescaleThreshold;
+      if (!__any_sync(0xffffffffu, need)) return true;
+      if (!o_ready && !__all_sync(0xffffffffu, mbar_wait(o_bar, o_parity, ctx, kStatusTimeoutO))) return false;
+      tc_fence_after();
+      const float f = need ? ex2_approx(m_run - m_new) : 1.0f;
+      if (need) {
+        l_run *= f;
+        m_run = m_new;
+      }
+#pragma unroll 1
+      for (int c16 = 0; c16 < 8; ++c16) {
+        uint32_t o[16];
+        tmem_ld16_wait(tO + c16 * 16, o);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+        tmem_st16(tO + c16 * 16, o);
+      }
+      tmem_st_wait();
+      return true;
+    };
+
     for (int j = 0; ok && j < n_kv; ++j) {
+      prof_mark<kProf>(p, rec, t, j, 0);
       ok = __all_sync(0xffffffffu, mbar_wait(bar(kBarSFull + t), uint32_t(j) & 1u, ctx, kStatusTimeoutS));
       if (!ok) break;
+      prof_mark<kProf>(p, rec, t, j, 1);
       tc_fence_after();
       uint32_t sa[64], sb[64];
       tmem_ld64_wait(tS, sa);
@@ -270,77 +383,58 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 128; ++i)
           if (i >= tail_valid) s[i] = -INFINITY;
       }
-      float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
-#pragma unroll
-      for (int i = 4; i < 128; i += 4) {
-        mx0 = fmaxf(mx0, s[i]);
-        mx1 = fmaxf(mx1, s[i + 1]);
-        mx2 = fmaxf(mx2, s[i + 2]);
-        mx3 = fmaxf(mx3, s[i + 3]);
+      prof_mark<kProf>(p, rec, t, j, 2);
+      if (kPingPong && (t == 1 || j > 0)) {
+        const uint32_t par = t == 0 ? uint32_t(j - 1) & 1u : uint32_t(j) & 1u;
+        ok = __all_sync(0xffffffffu, mbar_wait(bar(kBarTok + t), par, ctx, kStatusTimeoutS));
+        if (!ok) break;
       }
-      const float m_new = fmaxf(m_run, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * c);
-      if (j == 0) {
-        m_run = m_new;
-      } else {
-        const bool need = m_new > m_run + kRescaleThreshold;
-        if (__any_sync(0xffffffffu, need)) {
-          // O_t still holds the sum up to tile j-1: wait for that PV, then rescale in place.
-          ok = __all_sync(0xffffffffu,
-                          mbar_wait(bar(kBarODone + t), uint32_t(j - 1) & 1u, ctx, kStatusTimeoutO));
-          if (!ok) break;
-          tc_fence_after();
-          const float f = need ? ex2_approx(m_run - m_new) : 1.0f;
-          if (need) {
-            l_run *= f;
-            m_run = m_new;
-          }
-          // 16-column chunks keep this rare path within the register budget while s[] is live.
-#pragma unroll 1
-          for (int c16 = 0; c16 < 8; ++c16) {
-            uint32_t o[16];
-            tmem_ld16_wait(tO + c16 * 16, o);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
-            tmem_st16(tO + c16 * 16, o);
-          }
-          tmem_st_wait();
+      for (int h = 0; h < 2; ++h) {
+        // every half holds at least one live key except possibly the second half of the last tile
+        float mx0 = s[64 * h], mx1 = s[64 * h + 1], mx2 = s[64 * h + 2], mx3 = s[64 * h + 3];
+#pragma unroll
+        for (int i = 4; i < 64; i += 4) {
+          mx0 = fmaxf(mx0, s[64 * h + i]);
+          mx1 = fmaxf(mx1, s[64 * h + i + 1]);
+          mx2 = fmaxf(mx2, s[64 * h + i + 2]);
+          mx3 = fmaxf(mx3, s[64 * h + i + 3]);
         }
-      }
-      const float neg_m = -m_run;
-      float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
-      uint32_t pa[32], pb[32];
+        const float m_new = fmaxf(m_run, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * c);
+        if (j == 0 && h == 0) {
+          m_run = m_new;
+        } else if (h == 0) {
+          // S_t(j) ready implies every earlier P*V of this tile has retired
+          if (!(ok = rescale(m_new, 0, 0, true))) break;
+        } else {
+          if (!(ok = rescale(m_new, bar(kBarODoneA + t), uint32_t(j) & 1u, false))) break;
+        }
+        prof_mark<kProf>(p, rec, t, j, 3 + 2 * h);
+        const float neg_m = -m_run;
+        float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
+        uint32_t pk[32];
 #pragma unroll
-      for (int i = 0; i < 32; i += 2) {
-        const float e0 = ex2_approx(fmaf(s[2 * i], c, neg_m));
-        const float e1 = ex2_approx(fmaf(s[2 * i + 1], c, neg_m));
-        const float e2 = ex2_approx(fmaf(s[2 * i + 2], c, neg_m));
-        const float e3 = ex2_approx(fmaf(s[2 * i + 3], c, neg_m));
-        l0 += e0;
-        l1 += e1;
-        l2 += e2;
-        l3 += e3;
-        pa[i] = pack_bf16x2(e0, e1);
-        pa[i + 1] = pack_bf16x2(e2, e3);
+        for (int i = 0; i < 32; i += 2) {
+          const int e = 64 * h + 2 * i;
+          const float e0 = ex2_mixed<kEmu>(fmaf(s[e], c, neg_m), e);
+          const float e1 = ex2_mixed<kEmu>(fmaf(s[e + 1], c, neg_m), e + 1);
+          const float e2 = ex2_mixed<kEmu>(fmaf(s[e + 2], c, neg_m), e + 2);
+          const float e3 = ex2_mixed<kEmu>(fmaf(s[e + 3], c, neg_m), e + 3);
+          l0 += e0;
+          l1 += e1;
+          l2 += e2;
+          l3 += e3;
+          pk[i] = pack_bf16x2(e0, e1);
+          pk[i + 1] = pack_bf16x2(e2, e3);
+        }
+        if (kPingPong && h == 1) mbar_arrive(bar(kBarTok + (t ^ 1)));  // hand the exp phase over
+        l_run += (l0 + l1) + (l2 + l3);
+        tmem_st32(tP + 32 * h, pk);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(bar(h == 0 ? kBarPFullA + t : kBarPFullB + t));
+        prof_mark<kProf>(p, rec, t, j, 4 + 2 * h);
       }
-#pragma unroll
-      for (int i = 0; i < 32; i += 2) {
-        const float e0 = ex2_approx(fmaf(s[64 + 2 * i], c, neg_m));
-        const float e1 = ex2_approx(fmaf(s[64 + 2 * i + 1], c, neg_m));
-        const float e2 = ex2_approx(fmaf(s[64 + 2 * i + 2], c, neg_m));
-        const float e3 = ex2_approx(fmaf(s[64 + 2 * i + 3], c, neg_m));
-        l0 += e0;
-        l1 += e1;
-        l2 += e2;
-        l3 += e3;
-        pb[i] = pack_bf16x2(e0, e1);
-        pb[i + 1] = pack_bf16x2(e2, e3);
-      }
-      l_run += (l0 + l1) + (l2 + l3);
-      tmem_st32(tP, pa);
-      tmem_st32(tP + 32, pb);
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(bar(kBarPFull + t));
     }
     if (ok) {
       ok = __all_sync(0xffffffffu,
@@ -547,10 +641,23 @@ static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 using namespace h3::attn;
 
-extern "C" int h3_attn_fwd(const void* q, const void* k, const void* v, void* o, int64_t n_heads, int64_t s_q,
-                           int64_t s_kv, int64_t q_head_stride, int64_t q_row_stride, int64_t kv_head_stride,
-                           int64_t kv_row_stride, int64_t o_rank_rows, int64_t o_rank_stride, int64_t o_head_stride,
-                           int64_t o_row_stride, float softmax_scale, int32_t* status, void* stream) {
+template <bool kPingPong, int kEmu, bool kProf = false>
+static int launch_variant(dim3 grid, cudaStream_t st, const CUtensorMap& tq, const CUtensorMap& tk,
+                          const CUtensorMap& tv, const Params& p) {
+  auto* kern = attn_fwd_kernel<kPingPong, kEmu, kProf>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) != cudaSuccess)
+    return H3_ERR_LAUNCH;
+  kern<<<grid, kThreads, kSmemBytes, st>>>(tq, tk, tv, p);
+  return cudaGetLastError() == cudaSuccess ? H3_OK : H3_ERR_LAUNCH;
+}
+
+constexpr int kDefaultVariant = 0;
+
+static int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, int64_t n_heads, int64_t s_q,
+                         int64_t s_kv, int64_t q_head_stride, int64_t q_row_stride, int64_t kv_head_stride,
+                         int64_t kv_row_stride, int64_t o_rank_rows, int64_t o_rank_stride, int64_t o_head_stride,
+                         int64_t o_row_stride, float softmax_scale, int32_t* status, int32_t variant,
+                         long long* prof, int prof_iters, void* stream) {
   if (!q || !k || !v || !o || !status) return H3_ERR_NULL;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || (reinterpret_cast<uintptr_t>(status) & 3u))
     return H3_ERR_ALIGN;
@@ -585,13 +692,59 @@ extern "C" int h3_attn_fwd(const void* q, const void* k, const void* v, void* o,
   p.o_head_stride = o_head_stride;
   p.o_row_stride = o_row_stride;
   p.status = status;
+  p.prof = prof;
+  p.prof_iters = prof_iters;
 
-  if (cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) !=
-      cudaSuccess)
-    return H3_ERR_LAUNCH;
   dim3 grid((unsigned)((s_q + kRowsPerCta - 1) / kRowsPerCta), (unsigned)n_heads);
-  attn_fwd_kernel<<<grid, kThreads, kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
-  return cudaGetLastError() == cudaSuccess ? H3_OK : H3_ERR_LAUNCH;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (prof != nullptr) {
+    switch (variant) {
+      case 0: return launch_variant<false, 0, true>(grid, st, tq, tk, tv, p);
+      case 1: return launch_variant<true, 0, true>(grid, st, tq, tk, tv, p);
+      case 2: return launch_variant<true, 4, true>(grid, st, tq, tk, tv, p);
+      case 3: return launch_variant<true, 8, true>(grid, st, tq, tk, tv, p);
+      default: return H3_ERR_UNSUPPORTED;
+    }
+  }
+  switch (variant) {
+    case 0: return launch_variant<false, 0>(grid, st, tq, tk, tv, p);
+    case 1: return launch_variant<true, 0>(grid, st, tq, tk, tv, p);
+    case 2: return launch_variant<true, 4>(grid, st, tq, tk, tv, p);
+    case 3: return launch_variant<true, 8>(grid, st, tq, tk, tv, p);
+    case 4: return launch_variant<true, 2>(grid, st, tq, tk, tv, p);
+    default: return H3_ERR_UNSUPPORTED;
+  }
+}
+
+extern "C" int h3_attn_fwd_variant(const void* q, const void* k, const void* v, void* o, int64_t n_heads,
+                                   int64_t s_q, int64_t s_kv, int64_t q_head_stride, int64_t q_row_stride,
+                                   int64_t kv_head_stride, int64_t kv_row_stride, int64_t o_rank_rows,
+                                   int64_t o_rank_stride, int64_t o_head_stride, int64_t o_row_stride,
+                                   float softmax_scale, int32_t* status, int32_t variant, void* stream) {
+  return attn_fwd_impl(q, k, v, o, n_heads, s_q, s_kv, q_head_stride, q_row_stride, kv_head_stride, kv_row_stride,
+                       o_rank_rows, o_rank_stride, o_head_stride, o_row_stride, softmax_scale, status, variant,
+                       nullptr, 0, stream);
+}
+
+extern "C" int h3_attn_fwd_profile(const void* q, const void* k, const void* v, void* o, int64_t n_heads,
+                                   int64_t s_q, int64_t s_kv, int64_t q_head_stride, int64_t q_row_stride,
+                                   int64_t kv_head_stride, int64_t kv_row_stride, int64_t o_rank_rows,
+                                   int64_t o_rank_stride, int64_t o_head_stride, int64_t o_row_stride,
+                                   float softmax_scale, int32_t* status, int32_t variant, long long* trace,
+                                   int64_t trace_iters, void* stream) {
+  if (!trace || trace_iters < 1 || trace_iters > (1 << 20)) return H3_ERR_SHAPE;
+  return attn_fwd_impl(q, k, v, o, n_heads, s_q, s_kv, q_head_stride, q_row_stride, kv_head_stride, kv_row_stride,
+                       o_rank_rows, o_rank_stride, o_head_stride, o_row_stride, softmax_scale, status, variant, trace,
+                       (int)trace_iters, stream);
+}
+
+extern "C" int h3_attn_fwd(const void* q, const void* k, const void* v, void* o, int64_t n_heads, int64_t s_q,
+                           int64_t s_kv, int64_t q_head_stride, int64_t q_row_stride, int64_t kv_head_stride,
+                           int64_t kv_row_stride, int64_t o_rank_rows, int64_t o_rank_stride, int64_t o_head_stride,
+                           int64_t o_row_stride, float softmax_scale, int32_t* status, void* stream) {
+  return h3_attn_fwd_variant(q, k, v, o, n_heads, s_q, s_kv, q_head_stride, q_row_stride, kv_head_stride,
+                             kv_row_stride, o_rank_rows, o_rank_stride, o_head_stride, o_row_stride, softmax_scale,
+                             status, kDefaultVariant, stream);
 }
 
 extern "C" int h3_tile_kat_qk(const void* q, const void* k, float* s_out, int32_t* status, void* stream) {

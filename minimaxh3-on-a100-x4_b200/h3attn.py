@@ -58,6 +58,8 @@ def lib() -> ctypes.CDLL:
         L.h3_version.restype = ctypes.c_int
         L.h3_attn_fwd.argtypes = [vp, vp, vp, vp] + [i64] * 11 + [f32, i32p, vp]
         L.h3_attn_fwd.restype = ctypes.c_int
+        L.h3_attn_fwd_variant.argtypes = [vp, vp, vp, vp] + [i64] * 11 + [f32, i32p, ctypes.c_int32, vp]
+        L.h3_attn_fwd_variant.restype = ctypes.c_int
         L.h3_qknorm_rope_pack.argtypes = [vp, vp, vp, i64, vp, i64, vp, vp, f32, vp, vp, vp, i64, i64, i64, i64,
                                           i64, vp]
         L.h3_qknorm_rope_pack.restype = ctypes.c_int
@@ -115,7 +117,7 @@ def check_status(device=None) -> None:
 # ----------------------------------------------------------------------------- attention
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, s_kv: int | None = None,
               scale: float | None = None, out: torch.Tensor | None = None, layout: str = "head",
-              world: int = 1) -> torch.Tensor:
+              world: int = 1, variant: int | None = None) -> torch.Tensor:
     """Exact attention over heads: q [H, Sq, 128], k/v [H, Skv, 128] (bf16, last dim
     contiguous, any head/row strides that are multiples of 8). Keys/values stop at s_kv
     (default Skv). Output layout:
@@ -154,9 +156,13 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, s_kv: int | Non
         _cuda(out, "out")
         if tuple(out.shape) != tuple(shape) or not out.is_contiguous():
             raise H3Error(f"out must be contiguous {shape}, got {tuple(out.shape)}")
-    rc = lib().h3_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), H, sq, s_kv, q.stride(0),
-                           q.stride(1), k.stride(0), k.stride(1), rank_rows, rank_stride, head_stride, row_stride,
-                           scale, status_word(q.device).data_ptr(), _stream())
+    args = (q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), H, sq, s_kv, q.stride(0), q.stride(1),
+            k.stride(0), k.stride(1), rank_rows, rank_stride, head_stride, row_stride, scale,
+            status_word(q.device).data_ptr())
+    if variant is None:
+        rc = lib().h3_attn_fwd(*args, _stream())
+    else:
+        rc = lib().h3_attn_fwd_variant(*args, int(variant), _stream())
     _check(rc, "h3_attn_fwd")
     return out
 

@@ -162,3 +162,20 @@ def test_bad_arguments_rejected(cuda_dev):
         h3attn.attention(q.cpu(), q, q)
     with pytest.raises(h3attn.H3Error):
         h3attn.attention(q, q, q, layout="send", world=3)
+
+
+@pytest.mark.parametrize("variant", [0, 1, 2, 3, 4])
+def test_attention_variants_vs_oracle(cuda_dev, variant):
+    """Every kernel schedule meets the tolerance; the ping-pong schedule without FMA-pipe
+    exponentials is bit-identical to the free-running one (scheduling only)."""
+    import h3attn
+    H, S_real, S_pad = 2, 1001, 1004
+    q, k, v = _inputs(21, H, S_pad, cuda_dev)
+    qd, kd, vd = (_bf16(a, cuda_dev) for a in (q, k, v))
+    o = h3attn.attention(qd, kd, vd, s_kv=S_real, variant=variant)
+    h3attn.check_status()
+    ref = O.attention(q, k, v, s_kv=S_real)
+    err = np.abs(o.float().cpu().numpy() - ref)
+    assert err.max() < MAX_ABS and err.mean() < MEAN_ABS, (err.max(), err.mean())
+    if variant == 1:
+        assert torch.equal(o, h3attn.attention(qd, kd, vd, s_kv=S_real, variant=0))
