@@ -75,59 +75,74 @@ def profiled_traffic(name: str, seq: int, heads: int):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+    """nvidia-smi clocks and throttle reasons, sampled every 200 ms from before the warm-up
+    until after the timed region; summary() keeps the samples stamped inside the timed
+    window (mark_start / mark_end), falling back to the whole run when the window was too
+    short to catch one."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
+    Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, n_gpus: int):
         self.n = n_gpus
         self.proc = None
+        self.t_start = self.t_end = None
         self.path = os.path.join(ROOT, "gpurun_out", f"clocks_bench_{os.getpid()}.csv")
 
-    def __enter__(self):
+    def start(self):
         try:
             os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
                                           "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
-        except (OSError, FileNotFoundError):
+        except OSError:
             self.proc = None
         return self
 
-    def __exit__(self, *a):
+    def mark_start(self):
+        self.t_start = time.time()
+
+    def mark_end(self):
+        self.t_end = time.time()
+
+    def stop(self):
         if self.proc is not None:
+            time.sleep(0.25)  # one more sample after the window
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
             self.f.close()
-        return False
+
+    def _rows(self):
+        with open(self.path) as f:
+            for line in f:
+                c = [x.strip() for x in line.split(",")]
+                if len(c) < 10 or not c[1].isdigit() or int(c[1]) >= self.n:
+                    continue
+                try:
+                    ts = time.mktime(time.strptime(c[0].split(".")[0], "%Y/%m/%d %H:%M:%S"))
+                    ts += float("0." + c[0].split(".")[1]) if "." in c[0] else 0.0
+                    yield ts, float(c[2]), float(c[3]), c[6:10]
+                except ValueError:
+                    continue
 
     def summary(self):
         if self.proc is None or not os.path.exists(self.path):
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        with open(self.path) as f:
-            for line in f:
-                c = [x.strip() for x in line.split(",")]
-                if len(c) < 9 or not c[0].isdigit() or int(c[0]) >= self.n:
-                    continue
-                try:
-                    sm.append(float(c[1]))
-                    mx.append(float(c[2]))
-                except ValueError:
-                    continue
-                for nm, val in zip(names, c[5:9]):
-                    if val.lower() == "active":
-                        reasons.add(nm)
-        if not sm:
+        rows = list(self._rows())
+        win = [r for r in rows if self.t_start is not None and self.t_start - 0.2 <= r[0] <= self.t_end + 0.2]
+        scope = "timed region"
+        if not win:
+            win, scope = rows, "whole run (timed region shorter than the sampling period)"
+        if not win:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        reasons = sorted({nm for r in win for nm, val in zip(self.NAMES, r[3]) if val.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[1] for r in win), "sm_max_mhz": max(r[2] for r in win),
+                "reasons": reasons, "samples": len(win), "scope": scope}
 
 
 def cpu_sdpa_sample(s_kv: int, heads: int, rows: int, reps: int, threads: int):
@@ -184,6 +199,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
 
     dev = torch.device("cuda", local)
     S, H, W = args.seq, HEADS, world
+    sampler = ClockSampler(W).start() if rank == 0 else None  # started early: nvidia-smi needs ~1 s
     if S % W or H % W:
         raise SystemExit(f"seq {S} and heads {H} must divide by {W}")
     sl, hl = S // W, H // W
@@ -240,38 +256,67 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
 
     # ---- device-timed region
     ev_att.clear()
-    sampler = ClockSampler(W) if rank == 0 else None
-    if sampler:
-        sampler.__enter__()
     sync_all()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if sampler:
+        sampler.mark_start()
     t0.record()
     for _ in range(args.steps):
         layer(qkv, timed=True)
     t1.record()
     sync_all()
     if sampler:
-        sampler.__exit__()
+        sampler.mark_end()
+        sampler.stop()
     ms = max_over_ranks(t0.elapsed_time(t1) / args.steps)
     att_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in ev_att))
     h3attn.check_status()
 
-    # ---- end-to-end through the public API: pinned host input -> device -> layer -> host
+    # ---- end-to-end through the public API: every step copies its input from pinned host
+    # memory and reads its output back. Copies run on their own streams with two device
+    # buffers each way, so step i+1's upload and step i-1's readback overlap step i's layer.
     host_in = torch.empty(qkv.shape, dtype=qkv.dtype, pin_memory=True)
     host_in.copy_(qkv)
-    host_out = torch.empty((sl, H * D), dtype=torch.bfloat16, pin_memory=True)
-    dev_in = torch.empty_like(qkv)
-    e2e_steps = max(3, min(args.steps, 10))
-    layer(dev_in.copy_(host_in, non_blocking=True))
+    host_out = [torch.empty((sl, H * D), dtype=torch.bfloat16, pin_memory=True) for _ in range(2)]
+    dev_in = [torch.empty_like(qkv) for _ in range(2)]
+    dev_out = [torch.empty((sl, H * D), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    compute = torch.cuda.current_stream()
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    ev = lambda: torch.cuda.Event()
+    in_ready, in_free, done, out_free = ([ev() for _ in range(2)] for _ in range(4))
+    for b in range(2):
+        in_free[b].record(compute)
+        out_free[b].record(compute)
+
+    def e2e_steps(n):
+        for i in range(n):
+            b = i % 2
+            with torch.cuda.stream(s_in):
+                s_in.wait_event(in_free[b])
+                dev_in[b].copy_(host_in, non_blocking=True)
+                in_ready[b].record(s_in)
+            compute.wait_event(in_ready[b])
+            compute.wait_event(out_free[b])
+            layer(dev_in[b], out=dev_out[b])
+            in_free[b].record(compute)
+            done[b].record(compute)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(done[b])
+                host_out[b].copy_(dev_out[b], non_blocking=True)
+                out_free[b].record(s_out)
+        compute.wait_stream(s_in)
+        compute.wait_stream(s_out)
+
+    e2e_n = max(3, min(args.steps, 10))
+    e2e_steps(2)
     sync_all()
     t0.record()
-    for _ in range(e2e_steps):
-        dev_in.copy_(host_in, non_blocking=True)
-        o = layer(dev_in)
-        host_out.copy_(o, non_blocking=True)
+    e2e_steps(e2e_n)
     t1.record()
     sync_all()
-    e2e_ms = max_over_ranks(t0.elapsed_time(t1) / e2e_steps)
+    e2e_ms = max_over_ranks(t0.elapsed_time(t1) / e2e_n)
+    if not torch.equal(host_out[(e2e_n - 1) % 2], layer(qkv).cpu()):
+        raise SystemExit("end-to-end output differs from the device-resident run")
 
     if rank != 0:
         return

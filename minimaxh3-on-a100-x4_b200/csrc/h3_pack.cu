@@ -27,80 +27,109 @@ __device__ __forceinline__ uint4 f32_to_bf16x8(const float* f) {
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-// One 8-lane group per (token, tensor, head) row of 128 elements. Lane g of the group
-// holds elements [8g, 8g+8) and [64+8g, 64+8g+8), so every rotary pair (i, i+64) is
-// in one thread. Sum of squares: the lane's 16 squares in element order, then an
-// xor-butterfly over the group (distances 4, 2, 1). All products and sums are
-// separately rounded fp32 operations (no contraction) so the CPU restatement in
-// oracle/ reproduces every bit.
-__global__ void __launch_bounds__(256) qknorm_rope_pack_kernel(
-    const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v,
-    long long in_row_stride, const float* __restrict__ rope, long long rope_row_stride,
-    const __nv_bfloat16* __restrict__ qw, const __nv_bfloat16* __restrict__ kw, float eps,
-    __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ k_out, __nv_bfloat16* __restrict__ v_out,
-    long long s_l, int n_heads, int heads_per_rank, long long out_rank_stride, long long out_head_stride) {
-  const long long n_groups = s_l * 3ll * n_heads;
-  const long long gid_raw = (long long)blockIdx.x * (blockDim.x >> 3) + (threadIdx.x >> 3);
-  const bool live = gid_raw < n_groups;
-  const long long gid = live ? gid_raw : n_groups - 1;  // idle lanes still join the shuffles
-  const int g = threadIdx.x & 7;
-  const int h = (int)(gid % n_heads);
-  const long long tt = gid / n_heads;
-  const int tensor = (int)(tt % 3);
-  const long long tok = tt / 3;
-
-  const __nv_bfloat16* src = tensor == 0 ? q : (tensor == 1 ? k : v);
-  __nv_bfloat16* dst = tensor == 0 ? q_out : (tensor == 1 ? k_out : v_out);
-  const __nv_bfloat16* row = src + tok * in_row_stride + (long long)h * kD;
-  __nv_bfloat16* orow = dst + (long long)(h / heads_per_rank) * out_rank_stride +
-                        (long long)(h % heads_per_rank) * out_head_stride + tok * kD;
-
-  const uint4 u0 = __ldg(reinterpret_cast<const uint4*>(row + 8 * g));
-  const uint4 u1 = __ldg(reinterpret_cast<const uint4*>(row + 64 + 8 * g));
-  // v rows run the same (discarded) arithmetic so every lane of the warp reaches the
-  // shuffles below even when a warp mixes tensors (n_heads not a multiple of 4).
+// Per-row arithmetic of the fused pack. Lane g (0..7) of an 8-lane group holds elements
+// [8g, 8g+8) and [64+8g, 64+8g+8) of one 128-element head row, so every rotary pair
+// (i, i+64) is in one thread. Sum of squares: the lane's 16 squares in element order,
+// then an xor-butterfly over the group (distances 4, 2, 1). All products and sums are
+// separately rounded fp32 operations (no contraction) so the CPU restatement in oracle/
+// reproduces every bit. `m` holds the lane's 8 rotation matrices (m00, m01, m10, m11).
+__device__ __forceinline__ void norm_rope_row(const uint4& u0, const uint4& u1, const float (&wf)[16],
+                                              const float4 (&m)[8], bool has_rope, float eps, uint4& o0, uint4& o1) {
   float x[16];
   bf16x8_to_f32(u0, x);
   bf16x8_to_f32(u1, x + 8);
   float acc = __fmul_rn(x[0], x[0]);
 #pragma unroll
   for (int i = 1; i < 16; ++i) acc = __fadd_rn(acc, __fmul_rn(x[i], x[i]));
-  // 8-lane butterfly; the group is aligned to 8 lanes so xor stays inside it.
   const unsigned full = 0xffffffffu;
   acc = __fadd_rn(acc, __shfl_xor_sync(full, acc, 4));
   acc = __fadd_rn(acc, __shfl_xor_sync(full, acc, 2));
   acc = __fadd_rn(acc, __shfl_xor_sync(full, acc, 1));
   const float mean = __fmul_rn(acc, 0.0078125f);  // / 128, exact
   const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
-  const __nv_bfloat16* w = tensor == 0 ? qw : kw;
-  float y[16];
-  if (w != nullptr) {
-    float wf[16];
-    bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(w + 8 * g)), wf);
-    bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(w + 64 + 8 * g)), wf + 8);
+  float y[16];  // a missing weight is 1.0f: (x * r) * 1 == x * r exactly
 #pragma unroll
-    for (int i = 0; i < 16; ++i) y[i] = __fmul_rn(__fmul_rn(x[i], r), wf[i]);
-  } else {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) y[i] = __fmul_rn(x[i], r);
-  }
-  if (rope != nullptr) {
-    const float4* m = reinterpret_cast<const float4*>(rope + tok * rope_row_stride) + 8 * g;
+  for (int i = 0; i < 16; ++i) y[i] = __fmul_rn(__fmul_rn(x[i], r), wf[i]);
+  if (has_rope) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float4 mm = __ldg(m + i);  // (m00, m01, m10, m11) of pair 8g+i
       const float a = y[i], b = y[8 + i];
-      y[i] = __fadd_rn(__fmul_rn(mm.x, a), __fmul_rn(mm.y, b));
-      y[8 + i] = __fadd_rn(__fmul_rn(mm.z, a), __fmul_rn(mm.w, b));
+      y[i] = __fadd_rn(__fmul_rn(m[i].x, a), __fmul_rn(m[i].y, b));
+      y[8 + i] = __fadd_rn(__fmul_rn(m[i].z, a), __fmul_rn(m[i].w, b));
     }
   }
-  if (live) {
-    if (tensor == 2) {  // v: copied unchanged into the send layout
-      reinterpret_cast<uint4*>(orow + 8 * g)[0] = u0;
-      reinterpret_cast<uint4*>(orow + 64 + 8 * g)[0] = u1;
-    } else {
-      reinterpret_cast<uint4*>(orow + 8 * g)[0] = f32_to_bf16x8(y);
-      reinterpret_cast<uint4*>(orow + 64 + 8 * g)[0] = f32_to_bf16x8(y + 8);
+  o0 = f32_to_bf16x8(y);
+  o1 = f32_to_bf16x8(y + 8);
+}
+
+// One warp per token (grid-stride): the token's rotation table row (1 KB) is loaded into
+// registers once and reused for its q and k heads; the warp's four 8-lane groups walk the
+// token's 3*n_heads head rows, kRowsInFlight rows per group per step so that many 16-byte
+// load pairs per lane are in flight. v rows are copied unchanged. Every lane joins every shuffle (rows past
+// the end are clamped and not stored), so any n_heads works.
+constexpr int kRowsInFlight = 4;
+
+__global__ void __launch_bounds__(256, 2) qknorm_rope_pack_kernel(
+    const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v,
+    long long in_row_stride, const float* __restrict__ rope, long long rope_row_stride,
+    const __nv_bfloat16* __restrict__ qw, const __nv_bfloat16* __restrict__ kw, float eps,
+    __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ k_out, __nv_bfloat16* __restrict__ v_out,
+    long long s_l, int n_heads, int heads_per_rank, long long out_rank_stride, long long out_head_stride) {
+  const int lane = threadIdx.x & 31;
+  const int g = lane & 7;
+  const int grp = lane >> 3;
+  const long long warp_id = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const long long n_warps = ((long long)gridDim.x * blockDim.x) >> 5;
+  const int n_rows = 3 * n_heads;
+  for (long long tok = warp_id; tok < s_l; tok += n_warps) {
+    float4 m[8] = {};
+    if (rope != nullptr) {
+      const float4* mr = reinterpret_cast<const float4*>(rope + tok * rope_row_stride) + 8 * g;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) m[i] = __ldg(mr + i);
+    }
+    for (int base = 0; base < n_rows; base += 4 * kRowsInFlight) {
+      int rr[kRowsInFlight];
+      uint4 u[kRowsInFlight][2];
+#pragma unroll
+      for (int pr = 0; pr < kRowsInFlight; ++pr) {
+        const int r = base + 4 * pr + grp;
+        rr[pr] = r;
+        const int rc = r < n_rows ? r : n_rows - 1;
+        const int tensor = rc / n_heads, h = rc - tensor * n_heads;
+        const __nv_bfloat16* src = (tensor == 0 ? q : (tensor == 1 ? k : v)) + tok * in_row_stride + (long long)h * kD;
+        u[pr][0] = __ldg(reinterpret_cast<const uint4*>(src + 8 * g));
+        u[pr][1] = __ldg(reinterpret_cast<const uint4*>(src + 64 + 8 * g));
+      }
+#pragma unroll
+      for (int pr = 0; pr < kRowsInFlight; ++pr) {
+        const int r = rr[pr];
+        const int rc = r < n_rows ? r : n_rows - 1;
+        const int tensor = rc / n_heads, h = rc - tensor * n_heads;
+        uint4 o0, o1;
+        float wsel[16];  // this row's RMSNorm weight (L1-resident), 1.0 when absent
+        const __nv_bfloat16* w = tensor == 0 ? qw : kw;
+        if (w != nullptr) {
+          bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(w + 8 * g)), wsel);
+          bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(w + 64 + 8 * g)), wsel + 8);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) wsel[i] = 1.0f;
+        }
+        // v rows run the same (discarded) arithmetic so the warp stays converged for the shuffles
+        norm_rope_row(u[pr][0], u[pr][1], wsel, m, rope != nullptr, eps, o0, o1);
+        if (tensor == 2) {
+          o0 = u[pr][0];
+          o1 = u[pr][1];
+        }
+        if (r < n_rows) {
+          __nv_bfloat16* dst = (tensor == 0 ? q_out : (tensor == 1 ? k_out : v_out)) +
+                               (long long)(h / heads_per_rank) * out_rank_stride +
+                               (long long)(h % heads_per_rank) * out_head_stride + tok * kD;
+          reinterpret_cast<uint4*>(dst + 8 * g)[0] = o0;
+          reinterpret_cast<uint4*>(dst + 64 + 8 * g)[0] = o1;
+        }
+      }
     }
   }
 }
@@ -172,9 +201,8 @@ extern "C" int h3_qknorm_rope_pack(const void* q, const void* k, const void* v, 
       (rope && (rope_row_stride < 256 || (rope_row_stride % 4))))
     return H3_ERR_STRIDE;
   if (!(eps >= 0.f)) return H3_ERR_SHAPE;
-  const long long groups = s_l * 3 * n_heads;
-  const long long blocks = (groups + 31) / 32;  // 32 groups of 8 lanes per 256-thread block
-  if (blocks > 0x7fffffffll) return H3_ERR_SHAPE;
+  // one warp per token, 8 warps per block, grid-stride: up to 8 resident blocks per SM
+  const int blocks = grid_for(s_l, 8, 148 * 8);
   qknorm_rope_pack_kernel<<<(unsigned)blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const __nv_bfloat16*>(q), reinterpret_cast<const __nv_bfloat16*>(k),
       reinterpret_cast<const __nv_bfloat16*>(v), in_row_stride, rope, rope_row_stride,
