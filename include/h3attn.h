@@ -36,6 +36,8 @@ extern "C" {
 #define H3_ERR_DRIVER (-7)      /* driver entry point unavailable */
 #define H3_ERR_UNSUPPORTED (-8) /* a configuration this build does not implement */
 #define H3_ERR_CUDA (-9)        /* a CUDA runtime call failed (h3_status_read) */
+#define H3_ERR_SCRATCH_LIMIT (-10)  /* h3_attn_layer_noalloc: the call needs more than its static scratch */
+#define H3_ERR_DEVICE_TIMEOUT (-11) /* h3_attn_layer_noalloc: a kernel gave up waiting (bounded wait) */
 
 /* device status codes (positive, written by kernels into the status word) */
 #define H3_STATUS_OK 0
@@ -136,6 +138,21 @@ int h3_head_to_seq_unpack(const void* recv, void* out, int64_t n_heads, int64_t 
  *                   exactly as the softmax warps write P) */
 int h3_tile_kat_qk(const void* q, const void* k, float* s_out, int32_t* status, void* stream);
 int h3_tile_kat_pv(const void* p, const void* v, float* o_out, int32_t* status, void* stream);
+
+/* No counterpart in the reference. The single-GPU attention layer -- h3_qknorm_rope_pack into
+ * head-major q/k/v, then h3_attn_fwd into token-major o -- for callers that cannot allocate device
+ * memory themselves (e.g. C or FFI code inside an application whose caching allocator owns all device
+ * memory). The caller passes only inputs and outputs: qkv [s][3*n_heads*128] bf16 (q, k, v column
+ * blocks, row stride qkv_row_stride), rope fp32 [s][64][2][2] or NULL, bf16 weights or NULL,
+ * o [s][n_heads*128] bf16. The packed intermediate and the status word live in a static device array
+ * of 64 MiB + 256 B that every GPU loading the library keeps until exit; calls needing more
+ * (3*s*n_heads*128*2 bytes > 64 MiB, i.e. s*n_heads > 87381) return H3_ERR_SCRATCH_LIMIT. The first
+ * call on a device looks up the array's device address (make it before any stream capture on that
+ * device). All calls share the array, so calls that overlap on the GPU race. The call waits for
+ * `stream` to drain and returns H3_ERR_DEVICE_TIMEOUT if a kernel reported a bounded-wait timeout. */
+int h3_attn_layer_noalloc(const void* qkv, int64_t qkv_row_stride, const float* rope, int64_t rope_row_stride,
+                          const void* q_weight, const void* k_weight, float eps, void* o, int64_t s, int64_t n_heads,
+                          float softmax_scale, void* stream);
 
 /* Synchronise `stream`, then return the status word's value (>= 0), or H3_ERR_CUDA. */
 int h3_status_read(const int32_t* status, void* stream);
