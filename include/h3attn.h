@@ -78,6 +78,11 @@ int h3_attn_fwd(const void* q, const void* k, const void* v, void* o, int64_t n_
  *   2  ping-pong, every 4th element's exp2 on the FMA pipe (degree-3 minimax polynomial)
  *   3  ping-pong, every 8th element on the FMA pipe
  *   4  ping-pong, every 2nd element on the FMA pipe
+ *   5  four threads per query row (16-lane TMEM shapes), exp2 on MUFU
+ *   6  as 5 with the ping-pong token
+ *   7, 8, 9  as 5 with 1/8, 1/4, 1/2 of the keys' exp2 on the FMA pipe
+ *   10 as 0 with one MMA-issuing thread per Q tile; 11 as 10 with the ping-pong token;
+ *   12 as 10 with every 8th element's exp2 on the FMA pipe
  * Returns H3_ERR_UNSUPPORTED for any other value. */
 int h3_attn_fwd_variant(const void* q, const void* k, const void* v, void* o, int64_t n_heads, int64_t s_q,
                         int64_t s_kv, int64_t q_head_stride, int64_t q_row_stride, int64_t kv_head_stride,

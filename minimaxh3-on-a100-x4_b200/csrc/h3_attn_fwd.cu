@@ -29,7 +29,7 @@ constexpr int kD = 128;
 constexpr int kBlockM = 128;
 constexpr int kBlockN = 128;
 constexpr int kRowsPerCta = 2 * kBlockM;
-constexpr int kStages = 4;
+constexpr int kStages = 5;  // K/V ring: the MMA thread waits for V_j and K_{j+1} a full iteration ahead
 constexpr uint32_t kHalfBytes = 128u * 64u * 2u;  // 128 rows x 64 bf16: one 128-B swizzle column block
 constexpr uint32_t kTileBytes = 2u * kHalfBytes;  // 128 rows x 128 bf16
 constexpr int kThreads = 384;
@@ -111,15 +111,16 @@ __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t a_base, uint3
 }
 
 // O (+)= P V over 64 keys (half = 0: keys 0..63, half = 1: keys 64..127) of one tile: P
-// from TMEM (keys along columns, two bf16 per 32-bit column, 8 columns per K step), V
+// from TMEM (keys along columns, two bf16 per 32-bit column, 8 columns per K step; the
+// second half's P starts p_half_cols columns after the first's), V
 // MN-major in shared memory (d contiguous), two 64-wide d blocks 16 KB apart (LBO), 8-key
 // groups 1 KB apart (SBO); K steps advance 2 KB. `accumulate` applies to the first step.
 __device__ __forceinline__ void issue_pv_half(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_base, int half,
-                                              bool accumulate) {
+                                              bool accumulate, uint32_t p_half_cols = 32) {
   constexpr uint32_t idesc = idesc_bf16_f32(128, 128, 0, 1);
   const uint64_t bd = smem_desc_sw128(v_base + uint32_t(half) * 4u * 2048u, kHalfBytes, 1024);
   const uint32_t blo = uint32_t(bd), bhi = uint32_t(bd >> 32);
-  const uint32_t pa = p_tmem + uint32_t(half) * 32u;
+  const uint32_t pa = p_tmem + uint32_t(half) * p_half_cols;
 #define H3_PV_STEP(KK) \
   "add.u32 ta, %1, " #KK "*8;\n\t add.u32 lb, %2, " #KK "*128;\n\t mov.b64 db, {lb, %3};\n\t" \
   "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], db, %4, pt;\n\t"
@@ -179,7 +180,10 @@ __device__ __forceinline__ float ex2_mixed(float x, int idx) {
 // kPingPong: the two softmax warpgroups take turns (a token passed through two mbarriers)
 // for their exp phase, so one exponentiates while the tensor core runs the other's
 // P*V and next Q*K^T, instead of both contending for MUFU at once.
-template <bool kPingPong, int kEmu, bool kProf>
+// kDual: one MMA-issuing thread per Q tile (warps 1 and 3) instead of one for both, so a
+// tile's P*V never waits behind the other tile's P hand-off; shared K/V stages are released
+// by both (arrival count 2) and each thread's commits track only its own MMAs.
+template <bool kPingPong, int kEmu, bool kProf, bool kDual = false>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                     const __grid_constant__ CUtensorMap tmap_v, const Params p) {
@@ -201,7 +205,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bar(kBarQFull), 1);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(bar(kBarKVFull + s), 1);
-      mbar_init(bar(kBarKVEmpty + s), 1);
+      mbar_init(bar(kBarKVEmpty + s), kDual ? 2 : 1);
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(bar(kBarSFull + t), 1);
@@ -211,7 +215,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(kBarODone + t), 1);
       mbar_init(bar(kBarTok + t), 128);
     }
-    mbar_init(bar(kBarDrain), 1);
+    mbar_init(bar(kBarDrain), kDual ? 2 : 1);
     *abort_flag = (*reinterpret_cast<volatile int*>(p.status) != 0) ? 1 : 0;
     fence_mbar_init();
   }
@@ -265,7 +269,55 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (cnt > 0) drain_wait(bar(kBarKVFull + st), uint32_t(cnt - 1) & 1u, p.status);
       }
     }
-  } else if (warp == 1) {
+  } else if (kDual && (warp == 1 || warp == 3)) {
+    // ------------------------------------------------------------ MMA issuer for one Q tile
+    if (lane == 0 && !grid_aborted) {
+      const int t = warp == 1 ? 0 : 1;
+      const uint32_t sq = sbase + kOffQ + t * kTileBytes;
+      const uint32_t skv = sbase + kOffKV;
+      const bool rec = t == 0 && blockIdx.x == 0 && blockIdx.y == 0;
+      auto wait_full = [&](int st_it) -> bool {
+        return mbar_wait(bar(kBarKVFull + st_it % kStages), uint32_t(st_it / kStages) & 1u, ctx, kStatusTimeoutKV);
+      };
+      // smem operands arrive by TMA: the mbarrier wait orders them; the tcgen05 fence is only
+      // needed after waits on P, which other threads wrote with tcgen05.st.
+      bool ok = mbar_wait(bar(kBarQFull), 0, ctx, kStatusTimeoutQ) && wait_full(0);
+      if (ok) {
+        issue_qk(tmem + col_s(t), sq, skv);
+        mma_commit(bar(kBarSFull + t));
+        mma_commit(bar(kBarKVEmpty + 0));
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        prof_mark<kProf>(p, rec, 2, j, 0);
+        const int it_v = 2 * j + 1, it_k = 2 * j + 2;
+        const uint32_t ph = uint32_t(j) & 1u;
+        if (!(ok = wait_full(it_v))) break;
+        const uint32_t sv = skv + (it_v % kStages) * kTileBytes;
+        prof_mark<kProf>(p, rec, 2, j, 1);
+        if (!(ok = mbar_wait(bar(kBarPFullA + t), ph, ctx, kStatusTimeoutP))) break;
+        prof_mark<kProf>(p, rec, 2, j, 2);
+        tc_fence_after();
+        issue_pv_half(tmem + col_o(t), tmem + col_p(t), sv, 0, j > 0);
+        mma_commit(bar(kBarODoneA + t));
+        if (!(ok = mbar_wait(bar(kBarPFullB + t), ph, ctx, kStatusTimeoutP))) break;
+        prof_mark<kProf>(p, rec, 2, j, 3);
+        tc_fence_after();
+        issue_pv_half(tmem + col_o(t), tmem + col_p(t), sv, 1, true);
+        mma_commit(bar(kBarODone + t));
+        mma_commit(bar(kBarKVEmpty + it_v % kStages));
+        if (j + 1 < n_kv) {
+          if (!(ok = wait_full(it_k))) break;
+          prof_mark<kProf>(p, rec, 2, j, 4);
+          issue_qk(tmem + col_s(t), sq, skv + (it_k % kStages) * kTileBytes);
+          mma_commit(bar(kBarSFull + t));
+          mma_commit(bar(kBarKVEmpty + it_k % kStages));
+        }
+        prof_mark<kProf>(p, rec, 2, j, 5);
+      }
+      mma_commit(bar(kBarDrain));
+      drain_wait(bar(kBarDrain), 0, p.status);
+    }
+  } else if (!kDual && warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     // Ring order is K_0, V_0, K_1, V_1, ...; iteration j holds V_j and K_{j+1}. Both are
     // waited for before any P of iteration j, so no barrier wait sits between P_t * V_j
@@ -290,9 +342,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         prof_mark<kProf>(p, rec, 2, j, 0);
         const int it_v = 2 * j + 1, it_k = 2 * j + 2;
         const bool next = j + 1 < n_kv;
+        // smem operands arrive by TMA, ordered by the mbarrier wait alone; a tcgen05 fence is
+        // needed only after the waits on P, which other threads wrote with tcgen05.st.
         if (!(ok = wait_full(it_v))) break;
-        if (next && !(ok = wait_full(it_k))) break;
-        tc_fence_after();
         const uint32_t sv = skv + (it_v % kStages) * kTileBytes;
         const uint32_t sk = skv + (it_k % kStages) * kTileBytes;
         const uint32_t ph = uint32_t(j) & 1u;
@@ -310,6 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_commit(bar(kBarODone + t));
           if (t == 1) mma_commit(bar(kBarKVEmpty + it_v % kStages));
           if (next) {
+            if (t == 0 && !(ok = wait_full(it_k))) break;  // overlaps the queued P*V work
             issue_qk(tmem + col_s(t), sq + t * kTileBytes, sk);
             mma_commit(bar(kBarSFull + t));
             if (t == 1) mma_commit(bar(kBarKVEmpty + it_k % kStages));
@@ -468,6 +521,323 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------ kernel v2: four threads per row
+// 16 softmax warps (8 per Q tile) + TMA producer warp + MMA warp = 576 threads. Softmax warp w
+// covers TMEM lanes 32*(w&3) + 16*((w>>2)&1) .. +15 of tile w>>3 through the 16-lane shapes, so
+// each query row is held by a quad of threads (32 of its 128 keys each, as adjacent pairs) and
+// each thread holds two rows: row max/sum are two quad shuffles, and every thread's work per
+// KV tile is a quarter of a row-per-thread layout's, which shortens the softmax -> P*V -> next
+// Q*K^T chain that bounds the kernel. P of keys 0..63 goes to S columns 32..63, P of keys
+// 64..127 to columns 96..127 (each already consumed), so each 64-key half of S is loaded only
+// when it is processed.
+constexpr int kThreadsV2 = 576;
+constexpr int kWarpProducerV2 = 16;
+constexpr int kWarpMmaV2 = 17;
+
+template <bool kPingPong, int kEmu, bool kProf>
+__global__ void __launch_bounds__(kThreadsV2, 1)
+    attn_fwd_v2_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
+                       const __grid_constant__ CUtensorMap tmap_v, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBars);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int head = blockIdx.y;
+  const int m0 = blockIdx.x * kRowsPerCta;
+  const int n_kv = p.n_kv_tiles;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(kBarQFull), 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(bar(kBarKVFull + s), 1);
+      mbar_init(bar(kBarKVEmpty + s), 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(bar(kBarSFull + t), 1);
+      mbar_init(bar(kBarPFullA + t), 256);
+      mbar_init(bar(kBarPFullB + t), 256);
+      mbar_init(bar(kBarODoneA + t), 1);
+      mbar_init(bar(kBarODone + t), 1);
+      mbar_init(bar(kBarTok + t), 256);
+    }
+    mbar_init(bar(kBarDrain), 1);
+    *abort_flag = (*reinterpret_cast<volatile int*>(p.status) != 0) ? 1 : 0;
+    fence_mbar_init();
+  }
+  if (warp == kWarpProducerV2) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmap_q);
+      tma_prefetch_desc(&tmap_k);
+      tma_prefetch_desc(&tmap_v);
+    }
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const WaitCtx ctx{abort_flag, p.status};
+  const bool grid_aborted = *abort_flag != 0;
+
+  if (warp == kWarpProducerV2) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0 && !grid_aborted) {
+      const uint32_t sq = sbase + kOffQ;
+      const uint32_t skv = sbase + kOffKV;
+      mbar_expect_tx(bar(kBarQFull), 2 * kTileBytes);
+      for (int t = 0; t < 2; ++t)
+        for (int hh = 0; hh < 2; ++hh)
+          tma_load_3d(sq + t * kTileBytes + hh * kHalfBytes, &tmap_q, bar(kBarQFull), hh * 64, m0 + t * kBlockM,
+                      head);
+      int it = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        bool ok = true;
+        for (int kv = 0; kv < 2; ++kv, ++it) {
+          const int st = it % kStages;
+          const uint32_t ph = uint32_t(it / kStages) & 1u;
+          if (!mbar_wait(bar(kBarKVEmpty + st), ph ^ 1u, ctx, kStatusTimeoutKV)) {
+            ok = false;
+            break;
+          }
+          const CUtensorMap* m = kv ? &tmap_v : &tmap_k;
+          mbar_expect_tx(bar(kBarKVFull + st), kTileBytes);
+          tma_load_3d(skv + st * kTileBytes, m, bar(kBarKVFull + st), 0, j * kBlockN, head);
+          tma_load_3d(skv + st * kTileBytes + kHalfBytes, m, bar(kBarKVFull + st), 64, j * kBlockN, head);
+        }
+        if (!ok) break;
+      }
+      drain_wait(bar(kBarQFull), 0, p.status);
+      for (int st = 0; st < kStages; ++st) {
+        const int cnt = it / kStages + (st < it % kStages ? 1 : 0);
+        if (cnt > 0) drain_wait(bar(kBarKVFull + st), uint32_t(cnt - 1) & 1u, p.status);
+      }
+    }
+  } else if (warp == kWarpMmaV2) {
+    // ------------------------------------------------------------ MMA issuer (as in v1; P halves at S+32, S+96)
+    if (lane == 0 && !grid_aborted) {
+      const uint32_t sq = sbase + kOffQ;
+      const uint32_t skv = sbase + kOffKV;
+      const bool rec = blockIdx.x == 0 && blockIdx.y == 0;
+      auto wait_full = [&](int st_it) -> bool {
+        return mbar_wait(bar(kBarKVFull + st_it % kStages), uint32_t(st_it / kStages) & 1u, ctx, kStatusTimeoutKV);
+      };
+      bool ok = mbar_wait(bar(kBarQFull), 0, ctx, kStatusTimeoutQ) && wait_full(0);
+      if (ok) {
+        tc_fence_after();
+        issue_qk(tmem + col_s(0), sq, skv);
+        mma_commit(bar(kBarSFull + 0));
+        issue_qk(tmem + col_s(1), sq + kTileBytes, skv);
+        mma_commit(bar(kBarSFull + 1));
+        mma_commit(bar(kBarKVEmpty + 0));
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        prof_mark<kProf>(p, rec, 2, j, 0);
+        const int it_v = 2 * j + 1, it_k = 2 * j + 2;
+        const bool next = j + 1 < n_kv;
+        if (!(ok = wait_full(it_v))) break;  // TMA-fed smem: no tcgen05 fence needed
+        const uint32_t sv = skv + (it_v % kStages) * kTileBytes;
+        const uint32_t sk = skv + (it_k % kStages) * kTileBytes;
+        const uint32_t ph = uint32_t(j) & 1u;
+        prof_mark<kProf>(p, rec, 2, j, 1);
+        for (int t = 0; t < 2; ++t) {
+          if (!(ok = mbar_wait(bar(kBarPFullA + t), ph, ctx, kStatusTimeoutP))) break;
+          prof_mark<kProf>(p, rec, 2, j, 2 + 3 * t);
+          tc_fence_after();
+          issue_pv_half(tmem + col_o(t), tmem + col_s(t) + 32, sv, 0, j > 0, 64);
+          mma_commit(bar(kBarODoneA + t));
+          if (!(ok = mbar_wait(bar(kBarPFullB + t), ph, ctx, kStatusTimeoutP))) break;
+          prof_mark<kProf>(p, rec, 2, j, 3 + 3 * t);
+          tc_fence_after();
+          issue_pv_half(tmem + col_o(t), tmem + col_s(t) + 32, sv, 1, true, 64);
+          mma_commit(bar(kBarODone + t));
+          if (t == 1) mma_commit(bar(kBarKVEmpty + it_v % kStages));
+          if (next) {
+            if (t == 0 && !(ok = wait_full(it_k))) break;  // overlaps the queued P*V work
+            issue_qk(tmem + col_s(t), sq + t * kTileBytes, sk);
+            mma_commit(bar(kBarSFull + t));
+            if (t == 1) mma_commit(bar(kBarKVEmpty + it_k % kStages));
+          }
+          prof_mark<kProf>(p, rec, 2, j, 4 + 3 * t);
+        }
+      }
+      mma_commit(bar(kBarDrain));
+      drain_wait(bar(kBarDrain), 0, p.status);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue (warps 0..15)
+    const int t = warp >> 3;            // Q tile
+    const int hq = (warp >> 2) & 1;     // which 16 lanes of the quadrant
+    const int quad = warp & 3;          // TMEM lane quadrant this warp may access
+    const int t0 = lane & 3, t1 = lane >> 2;
+    const uint32_t lane_off = uint32_t(32 * quad + 16 * hq) << 16;
+    const uint32_t tS = tmem + lane_off + col_s(t);
+    const uint32_t tO = tmem + lane_off + col_o(t);
+    const float c = p.scale_log2;
+    const int tail_valid = p.s_kv - (n_kv - 1) * kBlockN;
+    float m_run[2] = {-INFINITY, -INFINITY};
+    float l_part[2] = {0.f, 0.f};  // this thread's share of each row's sum
+    bool ok = !grid_aborted;
+    const bool rec = blockIdx.x == 0 && blockIdx.y == 0 && warp == 8 * t && lane == 0;
+
+    auto rescale = [&](const float (&m_new)[2], uint32_t o_bar, uint32_t o_parity, bool o_ready) -> bool {
+      const bool need0 = m_new[0] > m_run[0] + kRescaleThreshold;
+      const bool need1 = m_new[1] > m_run[1] + kRescaleThreshold;
+      if (!__any_sync(0xffffffffu, need0 || need1)) return true;
+      if (!o_ready && !__all_sync(0xffffffffu, mbar_wait(o_bar, o_parity, ctx, kStatusTimeoutO))) return false;
+      tc_fence_after();
+      const float f0 = need0 ? ex2_approx(m_run[0] - m_new[0]) : 1.0f;
+      const float f1 = need1 ? ex2_approx(m_run[1] - m_new[1]) : 1.0f;
+      if (need0) {
+        l_part[0] *= f0;
+        m_run[0] = m_new[0];
+      }
+      if (need1) {
+        l_part[1] *= f1;
+        m_run[1] = m_new[1];
+      }
+#pragma unroll 1
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t o[16];
+        tmem_ld_16x256b_x4_wait(tO + c4 * 32, o);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * ((i & 2) ? f1 : f0));
+        tmem_st_16x256b_x4(tO + c4 * 32, o);
+      }
+      tmem_st_wait();
+      return true;
+    };
+
+    for (int j = 0; ok && j < n_kv; ++j) {
+      prof_mark<kProf>(p, rec, t, j, 0);
+      ok = __all_sync(0xffffffffu, mbar_wait(bar(kBarSFull + t), uint32_t(j) & 1u, ctx, kStatusTimeoutS));
+      if (!ok) break;
+      prof_mark<kProf>(p, rec, t, j, 1);
+      tc_fence_after();
+      if (kPingPong && (t == 1 || j > 0)) {
+        const uint32_t par = t == 0 ? uint32_t(j - 1) & 1u : uint32_t(j) & 1u;
+        ok = __all_sync(0xffffffffu, mbar_wait(bar(kBarTok + t), par, ctx, kStatusTimeoutS));
+        if (!ok) break;
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t sr[32];
+        tmem_ld_16x256b_x8_wait(tS + 64 * h, sr);
+        float s[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[i] = __uint_as_float(sr[i]);
+        if (j == n_kv - 1 && tail_valid < kBlockN) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int key = 64 * h + 8 * (i >> 2) + 2 * t0 + (i & 1);
+            if (key >= tail_valid) s[i] = -INFINITY;
+          }
+        }
+        if (h == 0) prof_mark<kProf>(p, rec, t, j, 2);
+        float mx0 = fmaxf(s[0], s[1]), mx1 = fmaxf(s[2], s[3]);
+#pragma unroll
+        for (int k = 1; k < 8; ++k) {
+          mx0 = fmaxf(mx0, fmaxf(s[4 * k], s[4 * k + 1]));
+          mx1 = fmaxf(mx1, fmaxf(s[4 * k + 2], s[4 * k + 3]));
+        }
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float m_new[2] = {fmaxf(m_run[0], mx0 * c), fmaxf(m_run[1], mx1 * c)};
+        if (j == 0 && h == 0) {
+          m_run[0] = m_new[0];
+          m_run[1] = m_new[1];
+        } else if (h == 0) {
+          if (!(ok = rescale(m_new, 0, 0, true))) break;  // S_t(j) ready: earlier P*V retired
+        } else {
+          if (!(ok = rescale(m_new, bar(kBarODoneA + t), uint32_t(j) & 1u, false))) break;
+        }
+        prof_mark<kProf>(p, rec, t, j, 3 + 2 * h);
+        const float nm0 = -m_run[0], nm1 = -m_run[1];
+        float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+        uint32_t pk[16];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          // FMA-pipe exp2 for the odd keys of selected repeats k: register slot (k, parity)
+          // holds key 64h + 8k + 2*t0 + parity for every t0, so the choice is a function of
+          // the key alone and each row's result stays independent of its position.
+          const bool poly = kEmu > 0 && (k % (kEmu > 1 ? kEmu / 2 : 1)) == (kEmu > 1 ? kEmu / 2 - 1 : 0);
+          const float e00 = ex2_approx(fmaf(s[4 * k], c, nm0));
+          const float e01 = poly ? ex2_poly(fmaf(s[4 * k + 1], c, nm0)) : ex2_approx(fmaf(s[4 * k + 1], c, nm0));
+          const float e10 = ex2_approx(fmaf(s[4 * k + 2], c, nm1));
+          const float e11 = poly ? ex2_poly(fmaf(s[4 * k + 3], c, nm1)) : ex2_approx(fmaf(s[4 * k + 3], c, nm1));
+          a0 += e00;
+          a1 += e01;
+          b0 += e10;
+          b1 += e11;
+          pk[2 * k] = pack_bf16x2(e00, e01);
+          pk[2 * k + 1] = pack_bf16x2(e10, e11);
+        }
+        if (kPingPong && h == 1) mbar_arrive(bar(kBarTok + (t ^ 1)));
+        l_part[0] += a0 + a1;
+        l_part[1] += b0 + b1;
+        tmem_st_16x128b_x8(tS + 32 + 64 * h, pk);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(bar(h == 0 ? kBarPFullA + t : kBarPFullB + t));
+        prof_mark<kProf>(p, rec, t, j, 4 + 2 * h);
+      }
+    }
+    if (ok) {
+      ok = __all_sync(0xffffffffu,
+                      mbar_wait(bar(kBarODone + t), uint32_t(n_kv - 1) & 1u, ctx, kStatusTimeoutO));
+    }
+    if (ok) {
+      tc_fence_after();
+      float l0 = l_part[0], l1 = l_part[1];
+      l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+      l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+      const float inv[2] = {1.0f / l0, 1.0f / l1};
+      __nv_bfloat16* dst[2];
+      bool valid[2];
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const int row = m0 + t * kBlockM + 32 * quad + 16 * hq + t1 + 8 * r;
+        valid[r] = row < p.s_q;
+        const long long rr = valid[r] ? row : 0;
+        dst[r] = p.o + (rr / p.o_rank_rows) * p.o_rank_stride + (long long)head * p.o_head_stride +
+                 (rr % p.o_rank_rows) * p.o_row_stride;
+      }
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t o[16];
+        tmem_ld_16x256b_x4_wait(tO + c4 * 32, o);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int col = 32 * c4 + 8 * k + 2 * t0;
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            const uint32_t w = pack_bf16x2(__uint_as_float(o[4 * k + 2 * r]) * inv[r],
+                                           __uint_as_float(o[4 * k + 2 * r + 1]) * inv[r]);
+            if (valid[r]) *reinterpret_cast<uint32_t*>(dst[r] + col) = w;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kWarpProducerV2) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -641,13 +1011,23 @@ static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 using namespace h3::attn;
 
-template <bool kPingPong, int kEmu, bool kProf = false>
+template <bool kPingPong, int kEmu, bool kProf = false, bool kDual = false>
 static int launch_variant(dim3 grid, cudaStream_t st, const CUtensorMap& tq, const CUtensorMap& tk,
                           const CUtensorMap& tv, const Params& p) {
-  auto* kern = attn_fwd_kernel<kPingPong, kEmu, kProf>;
+  auto* kern = attn_fwd_kernel<kPingPong, kEmu, kProf, kDual>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) != cudaSuccess)
     return H3_ERR_LAUNCH;
   kern<<<grid, kThreads, kSmemBytes, st>>>(tq, tk, tv, p);
+  return cudaGetLastError() == cudaSuccess ? H3_OK : H3_ERR_LAUNCH;
+}
+
+template <bool kPingPong, int kEmu, bool kProf = false>
+static int launch_v2(dim3 grid, cudaStream_t st, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                     const Params& p) {
+  auto* kern = attn_fwd_v2_kernel<kPingPong, kEmu, kProf>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) != cudaSuccess)
+    return H3_ERR_LAUNCH;
+  kern<<<grid, kThreadsV2, kSmemBytes, st>>>(tq, tk, tv, p);
   return cudaGetLastError() == cudaSuccess ? H3_OK : H3_ERR_LAUNCH;
 }
 
@@ -703,10 +1083,23 @@ static int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, i
       case 1: return launch_variant<true, 0, true>(grid, st, tq, tk, tv, p);
       case 2: return launch_variant<true, 4, true>(grid, st, tq, tk, tv, p);
       case 3: return launch_variant<true, 8, true>(grid, st, tq, tk, tv, p);
+      case 5: return launch_v2<false, 0, true>(grid, st, tq, tk, tv, p);
+      case 6: return launch_v2<true, 0, true>(grid, st, tq, tk, tv, p);
+      case 8: return launch_v2<false, 4, true>(grid, st, tq, tk, tv, p);
+      case 10: return launch_variant<false, 0, true, true>(grid, st, tq, tk, tv, p);
+      case 11: return launch_variant<true, 0, true, true>(grid, st, tq, tk, tv, p);
       default: return H3_ERR_UNSUPPORTED;
     }
   }
   switch (variant) {
+    case 5: return launch_v2<false, 0>(grid, st, tq, tk, tv, p);
+    case 6: return launch_v2<true, 0>(grid, st, tq, tk, tv, p);
+    case 7: return launch_v2<false, 8>(grid, st, tq, tk, tv, p);
+    case 8: return launch_v2<false, 4>(grid, st, tq, tk, tv, p);
+    case 9: return launch_v2<false, 2>(grid, st, tq, tk, tv, p);
+    case 10: return launch_variant<false, 0, false, true>(grid, st, tq, tk, tv, p);
+    case 11: return launch_variant<true, 0, false, true>(grid, st, tq, tk, tv, p);
+    case 12: return launch_variant<false, 8, false, true>(grid, st, tq, tk, tv, p);
     case 0: return launch_variant<false, 0>(grid, st, tq, tk, tv, p);
     case 1: return launch_variant<true, 0>(grid, st, tq, tk, tv, p);
     case 2: return launch_variant<true, 4>(grid, st, tq, tk, tv, p);
