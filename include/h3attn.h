@@ -143,6 +143,11 @@ int h3_head_to_seq_unpack(const void* recv, void* out, int64_t n_heads, int64_t 
  *                   exactly as the softmax warps write P) */
 int h3_tile_kat_qk(const void* q, const void* k, float* s_out, int32_t* status, void* stream);
 int h3_tile_kat_pv(const void* p, const void* v, float* o_out, int32_t* status, void* stream);
+/* The same through an SM pair (tcgen05.mma.cta_group::2, M = 256, two-CTA cluster):
+ *   h3_tile_kat_pair_qk: s_out[256][128] = q[256][128] . k[128][128]^T (CTA r: q rows 128r.., keys 64r..)
+ *   h3_tile_kat_pair_pv: o_out[256][128] = p[256][128] . v[128][128]   (CTA r: p rows 128r.., v cols 64r..) */
+int h3_tile_kat_pair_qk(const void* q, const void* k, float* s_out, int32_t* status, void* stream);
+int h3_tile_kat_pair_pv(const void* p, const void* v, float* o_out, int32_t* status, void* stream);
 
 /* No counterpart in the reference. The single-GPU attention layer -- h3_qknorm_rope_pack into
  * head-major q/k/v, then h3_attn_fwd into token-major o -- for callers that cannot allocate device

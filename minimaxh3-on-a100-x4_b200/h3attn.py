@@ -71,6 +71,9 @@ def lib() -> ctypes.CDLL:
         L.h3_tile_kat_qk.restype = ctypes.c_int
         L.h3_tile_kat_pv.argtypes = [vp, vp, vp, i32p, vp]
         L.h3_tile_kat_pv.restype = ctypes.c_int
+        for name in ("h3_tile_kat_pair_qk", "h3_tile_kat_pair_pv"):
+            getattr(L, name).argtypes = [vp, vp, vp, i32p, vp]
+            getattr(L, name).restype = ctypes.c_int
         L.h3_status_read.argtypes = [i32p, vp]
         L.h3_status_read.restype = ctypes.c_int
         _lib = L
@@ -271,4 +274,26 @@ def tile_kat_pv(p: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
     o = torch.empty((128, 128), dtype=torch.float32, device=p.device)
     _check(lib().h3_tile_kat_pv(p.data_ptr(), v.data_ptr(), o.data_ptr(), status_word(p.device).data_ptr(),
                                 _stream()), "h3_tile_kat_pv")
+    return o
+
+
+def tile_kat_pair_qk(q: torch.Tensor, k: torch.Tensor) -> torch.Tensor:
+    """S[256][128] = q[256][128] . k[128][128]^T through an SM pair (cta_group::2)."""
+    _cuda(q, "q")
+    _cuda(k, "k")
+    assert q.shape == (256, 128) and k.shape == (128, 128) and q.is_contiguous() and k.is_contiguous()
+    s = torch.empty((256, 128), dtype=torch.float32, device=q.device)
+    _check(lib().h3_tile_kat_pair_qk(q.data_ptr(), k.data_ptr(), s.data_ptr(), status_word(q.device).data_ptr(),
+                                     _stream()), "h3_tile_kat_pair_qk")
+    return s
+
+
+def tile_kat_pair_pv(p: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    """O[256][128] = p[256][128] . v[128][128] through an SM pair (cta_group::2)."""
+    _cuda(p, "p")
+    _cuda(v, "v")
+    assert p.shape == (256, 128) and v.shape == (128, 128) and p.is_contiguous() and v.is_contiguous()
+    o = torch.empty((256, 128), dtype=torch.float32, device=p.device)
+    _check(lib().h3_tile_kat_pair_pv(p.data_ptr(), v.data_ptr(), o.data_ptr(), status_word(p.device).data_ptr(),
+                                     _stream()), "h3_tile_kat_pair_pv")
     return o

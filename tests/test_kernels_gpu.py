@@ -58,6 +58,28 @@ def test_tile_kat_pv(cuda_dev):
     assert err.max().item() < 1e-3, err.max().item()
 
 
+def test_tile_kat_pair_qk(cuda_dev):
+    import h3attn
+    g = torch.Generator(device="cpu").manual_seed(2)
+    q = torch.randn(256, 128, generator=g).to(torch.bfloat16)
+    k = torch.randn(128, 128, generator=g).to(torch.bfloat16)
+    s = h3attn.tile_kat_pair_qk(q.to(cuda_dev), k.to(cuda_dev))
+    h3attn.check_status()
+    err = (s.cpu().double() - q.double() @ k.double().T).abs()
+    assert err.max().item() < 1e-3, err.max().item()
+
+
+def test_tile_kat_pair_pv(cuda_dev):
+    import h3attn
+    g = torch.Generator(device="cpu").manual_seed(3)
+    p = torch.rand(256, 128, generator=g).to(torch.bfloat16)
+    v = torch.randn(128, 128, generator=g).to(torch.bfloat16)
+    o = h3attn.tile_kat_pair_pv(p.to(cuda_dev), v.to(cuda_dev))
+    h3attn.check_status()
+    err = (o.cpu().double() - p.double() @ v.double()).abs()
+    assert err.max().item() < 1e-3, err.max().item()
+
+
 @pytest.mark.parametrize("H,S", [(2, 1), (2, 15), (2, 127), (2, 128), (2, 129), (2, 255), (2, 256), (3, 300),
                                  (2, 1000), (1, 4095)])
 def test_attention_vs_oracle(cuda_dev, H, S):
