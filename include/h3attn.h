@@ -83,6 +83,11 @@ int h3_attn_fwd(const void* q, const void* k, const void* v, void* o, int64_t n_
  *   7, 8, 9  as 5 with 1/8, 1/4, 1/2 of the keys' exp2 on the FMA pipe
  *   10 as 0 with one MMA-issuing thread per Q tile; 11 as 10 with the ping-pong token;
  *   12 as 10 with every 8th element's exp2 on the FMA pipe
+ *   13 SM-pair kernel: two-CTA clusters, cta_group::2 MMAs (each SM reads half of every K/V
+ *      tile), one 128-row Q tile per CTA with S double-buffered in TMEM
+ *   14 as 13 with two softmax warps per TMEM lane quarter, each owning 64 keys of every row
+ *   15 as 13 with two softmax warps per TMEM lane quarter, each owning 16 rows (four
+ *      threads per row)
  * Returns H3_ERR_UNSUPPORTED for any other value. */
 int h3_attn_fwd_variant(const void* q, const void* k, const void* v, void* o, int64_t n_heads, int64_t s_q,
                         int64_t s_kv, int64_t q_head_stride, int64_t q_row_stride, int64_t kv_head_stride,
@@ -90,7 +95,7 @@ int h3_attn_fwd_variant(const void* q, const void* k, const void* v, void* o, in
                         int64_t o_row_stride, float softmax_scale, int32_t* status, int32_t variant, void* stream);
 
 /* Phase profiler (diagnostics; cf. the clock64 phase counters of the reference kernel,
- * attn_sm80/fa3_sm80_h3.cu:96-105, :572-582): runs variant 0-3 and records clock64()
+ * attn_sm80/fa3_sm80_h3.cu:96-105, :572-582): runs variants 0-3, 5, 6, 8, 10, 11 or 13-15 and records clock64()
  * stamps of CTA (0, 0) for the first trace_iters KV iterations into the device buffer
  *   trace[((role * trace_iters) + j) * 8 + point]   (int64, 3 * trace_iters * 8 entries)
  * role 0/1 = softmax warpgroup of Q tile 0/1: points 0 before the S wait, 1 S ready,

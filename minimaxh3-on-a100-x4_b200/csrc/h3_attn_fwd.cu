@@ -23,9 +23,14 @@
 #include <cstdio>
 
 namespace h3 {
+namespace pair {
+int launch_attn(const void* q, const void* k, const void* v, void* o, long long n_heads, long long s_q, long long s_kv,
+                long long q_head_stride, long long q_row_stride, long long kv_head_stride, long long kv_row_stride,
+                long long o_rank_rows, long long o_rank_stride, long long o_head_stride, long long o_row_stride,
+                float scale_log2, int* status, int variant, long long* prof, int prof_iters, cudaStream_t st);
+}  // namespace pair
 namespace attn {
 
-constexpr int kD = 128;
 constexpr int kBlockM = 128;
 constexpr int kBlockN = 128;
 constexpr int kRowsPerCta = 2 * kBlockM;
@@ -149,25 +154,6 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, int* s
       return;
     }
   }
-}
-
-// 2^x on the FMA pipe (relieves MUFU): n = round(x) through the 1.5*2^23 shifter,
-// f = x - n in [-1/2, 1/2], 2^f by a degree-3 polynomial with minimax relative error
-// 7.5e-5 (Remez fit, csrc/gen_exp2_poly.py), n added straight into the exponent field.
-// x < -125 returns 0 (masked keys stay exactly zero; results stay normal numbers). The operation order is fixed,
-// so results do not depend on launch shape.
-__device__ __forceinline__ float ex2_poly(float x) {
-  const float shifter = 12582912.0f;  // 1.5 * 2^23
-  const float xc = fmaxf(x, -125.0f);
-  const float t = __fadd_rn(xc, shifter);
-  const float n = __fsub_rn(t, shifter);
-  const float f = __fsub_rn(xc, n);
-  float q = __fmaf_rn(5.517166853e-02f, f, 2.426111251e-01f);
-  q = __fmaf_rn(q, f, 6.932609677e-01f);
-  q = __fmaf_rn(q, f, 9.999280572e-01f);
-  const int ni = __float_as_int(t) - 0x4B400000;
-  const float r = __int_as_float(__float_as_int(q) + (ni << 23));
-  return x < -125.0f ? 0.0f : r;
 }
 
 // Element idx of a row takes the FMA-pipe exp2 when kEmu > 0 and idx % kEmu == kEmu - 1.
@@ -1052,9 +1038,14 @@ static int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, i
   if (!(softmax_scale > 0.f) || !std::isfinite(softmax_scale)) return H3_ERR_SHAPE;
   if (n_heads > 1 && (q_head_stride == 0 || kv_head_stride == 0)) return H3_ERR_STRIDE;
 
-  CUtensorMap tq, tk, tv;
   const long long qhs = n_heads > 1 ? q_head_stride : s_q * q_row_stride;
   const long long kvhs = n_heads > 1 ? kv_head_stride : s_kv * kv_row_stride;
+  if (variant >= 13 && variant <= 15)
+    return h3::pair::launch_attn(q, k, v, o, n_heads, s_q, s_kv, qhs, q_row_stride, kvhs, kv_row_stride, o_rank_rows,
+                                 o_rank_stride, o_head_stride, o_row_stride,
+                                 (float)((double)softmax_scale * 1.4426950408889634), status, variant, prof, prof_iters,
+                                 reinterpret_cast<cudaStream_t>(stream));
+  CUtensorMap tq, tk, tv;
   int rc;
   if ((rc = make_head_map(&tq, q, s_q, n_heads, q_row_stride, qhs)) != H3_OK) return rc;
   if ((rc = make_head_map(&tk, k, s_kv, n_heads, kv_row_stride, kvhs)) != H3_OK) return rc;

@@ -294,9 +294,25 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-// Arrive on an mbarrier of another CTA in the cluster (release at cluster scope).
+// Arrive on an mbarrier of another CTA in the cluster. Release at CTA scope: what the arrival
+// publishes here is tensor-memory state, ordered by tcgen05.wait::st and
+// tcgen05.fence::before_thread_sync ahead of it; a cluster-scope release costs ~1000 cycles
+// (it waits out the thread's outstanding global writes) and orders nothing more that matters.
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// Named barrier over n_threads (whole warps) returning the AND of every thread's `v`.
+__device__ __forceinline__ bool named_bar_and(int id, int n_threads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(r)
+      : "r"(uint32_t(v)), "r"(id), "r"(n_threads)
+      : "memory");
+  return r != 0;
 }
 __device__ __forceinline__ bool mbar_try_wait_acq_cluster(uint32_t bar, uint32_t parity) {
   uint32_t ok;
@@ -358,6 +374,25 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t bar, uint16_t cta_mask)
 }
 
 // ---------------------------------------------------------------- math
+// 2^x on the FMA pipe (relieves MUFU): n = round(x) through the 1.5*2^23 shifter,
+// f = x - n in [-1/2, 1/2], 2^f by a degree-3 polynomial with minimax relative error
+// 7.5e-5 (Remez fit, csrc/gen_exp2_poly.py), n added straight into the exponent field.
+// x < -125 returns 0 (masked keys stay exactly zero; results stay normal numbers). The operation order is fixed,
+// so results do not depend on launch shape.
+__device__ __forceinline__ float ex2_poly(float x) {
+  const float shifter = 12582912.0f;  // 1.5 * 2^23
+  const float xc = fmaxf(x, -125.0f);
+  const float t = __fadd_rn(xc, shifter);
+  const float n = __fsub_rn(t, shifter);
+  const float f = __fsub_rn(xc, n);
+  float q = __fmaf_rn(5.517166853e-02f, f, 2.426111251e-01f);
+  q = __fmaf_rn(q, f, 6.932609677e-01f);
+  q = __fmaf_rn(q, f, 9.999280572e-01f);
+  const int ni = __float_as_int(t) - 0x4B400000;
+  const float r = __int_as_float(__float_as_int(q) + (ni << 23));
+  return x < -125.0f ? 0.0f : r;
+}
+
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

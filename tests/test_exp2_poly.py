@@ -1,4 +1,4 @@
-"""The FMA-pipe exp2 of the attention kernel (ex2_poly in h3_attn_fwd.cu), emulated
+"""The FMA-pipe exp2 of the attention kernel (ex2_poly in h3_ptx.cuh), emulated
 operation by operation in fp32: relative error well under bf16's rounding step, exact
 zero below the clamp, and the coefficient derivation reproduces the constants used."""
 import os
@@ -14,8 +14,9 @@ f32 = np.float32
 
 
 def _coeffs():
-    src = open(os.path.join(CSRC, "h3_attn_fwd.cu")).read()
-    body = src[src.index("float ex2_poly("):src.index("template <int kEmu>")]
+    src = open(os.path.join(CSRC, "h3_ptx.cuh")).read()
+    start = src.index("float ex2_poly(")
+    body = src[start:src.index("\n}\n", start)]
     return [f32(x) for x in re.findall(r"(-?\d\.\d+e[-+]\d+)f", body)]
 
 

@@ -186,7 +186,7 @@ def test_bad_arguments_rejected(cuda_dev):
         h3attn.attention(q, q, q, layout="send", world=3)
 
 
-@pytest.mark.parametrize("variant", [0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12])
+@pytest.mark.parametrize("variant", [0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15])
 def test_attention_variants_vs_oracle(cuda_dev, variant):
     """Every kernel schedule meets the tolerance; the ping-pong schedule without FMA-pipe
     exponentials is bit-identical to the free-running one (scheduling only)."""
@@ -209,3 +209,27 @@ def test_attention_variants_vs_oracle(cuda_dev, variant):
     sub = h3attn.attention(qd[:, 129:700], kd, vd, s_kv=S_real, variant=variant)
     torch.cuda.synchronize()
     assert torch.equal(sub, o[:, 129:700])
+
+
+@pytest.mark.parametrize("H,S", [(2, 1), (2, 100), (2, 128), (2, 129), (2, 256), (2, 257), (3, 300), (2, 513),
+                                 (1, 1000)])
+@pytest.mark.parametrize("variant", [13, 14, 15])
+def test_pair_kernel_vs_oracle(cuda_dev, H, S, variant):
+    """The SM-pair kernels (variants 13-15) over ragged sizes: a pair whose second CTA has no rows
+    (S <= 128 + 256k), a lone key tile, odd tails; rows past S are never written."""
+    import h3attn
+    q, k, v = _inputs(31 + S, H, S, cuda_dev)
+    qd, kd, vd = (_bf16(a, cuda_dev) for a in (q, k, v))
+    out = torch.full((H, S + 8, 128), 7.0, dtype=torch.bfloat16, device=cuda_dev)
+    rc = h3attn.lib().h3_attn_fwd_variant(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), out.data_ptr(), H, S, S,
+                                          qd.stride(0), qd.stride(1), kd.stride(0), kd.stride(1), S, 0,
+                                          (S + 8) * 128, 128, 128 ** -0.5, h3attn.status_word(cuda_dev).data_ptr(),
+                                          variant, torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, rc
+    torch.cuda.synchronize()
+    h3attn.check_status()
+    o = out[:, :S]
+    ref = O.attention(q, k, v)
+    err = np.abs(o.float().cpu().numpy() - ref)
+    assert err.max() < MAX_ABS and err.mean() < MEAN_ABS, (err.max(), err.mean())
+    assert bool((out[:, S:] == 7.0).all())
