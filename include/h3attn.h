@@ -142,6 +142,24 @@ int h3_seq_to_head_unpack(const void* recv, void* out, int64_t world, int64_t he
  * applied to the head->seq all-to-all receive buffer (:76-77). */
 int h3_head_to_seq_unpack(const void* recv, void* out, int64_t n_heads, int64_t s_l, void* stream);
 
+/* Row-independent projection GEMM, bf16 in, fp32 accumulate, bf16 out:
+ *   epilogue 0: c[m][n] = sum_k a[m][k] * w[n][k]                  (w has n_out rows)
+ *   epilogue 1: c[m][n] = silu(a . w[n]) * (a . w[n_out + n])       (w = [gate; up], 2*n_out rows;
+ *               both products and silu rounded to bf16 as the host model's fc1 -> chunk -> silu -> mul)
+ * Replaces the projection linears around the attention op: qkv_proj (harness/sp_runtime.py:91) and
+ * out_proj (:126), and the FFN's fc1 and swiglu-into-fc2 linears (harness/sp_blockloop.py:169-170).
+ * w is an nn.Linear weight [out][in] (row stride w_row_stride). a is read as [a_chunks][m][a_chunk_cols]
+ * (element strides a_chunk_stride, a_row_stride) and multiplied as the row-major [m][a_chunks*a_chunk_cols]
+ * matrix: a_chunks = 1 is a plain row-major a; a_chunks = H, a_chunk_cols = 128 reads the head->seq
+ * receive buffer [H][s_l][128] in place (no unpack pass). Each output row is computed by one tile with
+ * one fixed reduction order, so the bits of a row do not depend on m or on the row's position: token
+ * shards on W ranks reproduce the 1-GPU result exactly. Requires 16-byte aligned pointers, strides and
+ * a_chunk_cols multiples of 8, a_chunk_cols a multiple of 64 when a_chunks > 1, n_out a multiple of 8
+ * (of 128 for epilogue 1). Allocates nothing. */
+int h3_gemm_bf16(const void* a, int64_t m, int64_t a_chunks, int64_t a_chunk_cols, int64_t a_chunk_stride,
+                 int64_t a_row_stride, const void* w, int64_t n_out, int64_t w_row_stride, void* c,
+                 int64_t c_row_stride, int32_t epilogue, int32_t* status, void* stream);
+
 /* Tile known-answer tests of the tcgen05 path (cf. attn_sm80/microtest.py:10-26):
  *   h3_tile_kat_qk: s_out[128][128] fp32 = q[128][128] . k[128][128]^T
  *   h3_tile_kat_pv: o_out[128][128] fp32 = p[128][128] . v[128][128]  (p written to TMEM

@@ -74,6 +74,8 @@ def lib() -> ctypes.CDLL:
         for name in ("h3_tile_kat_pair_qk", "h3_tile_kat_pair_pv"):
             getattr(L, name).argtypes = [vp, vp, vp, i32p, vp]
             getattr(L, name).restype = ctypes.c_int
+        L.h3_gemm_bf16.argtypes = [vp, i64, i64, i64, i64, i64, vp, i64, i64, vp, i64, ctypes.c_int32, i32p, vp]
+        L.h3_gemm_bf16.restype = ctypes.c_int
         L.h3_status_read.argtypes = [i32p, vp]
         L.h3_status_read.restype = ctypes.c_int
         _lib = L
@@ -253,6 +255,52 @@ def head_to_seq_unpack(recv: torch.Tensor, out: torch.Tensor | None = None) -> t
         raise H3Error("out has the wrong shape")
     rc = lib().h3_head_to_seq_unpack(recv.data_ptr(), out.data_ptr(), H, sl, _stream())
     _check(rc, "h3_head_to_seq_unpack")
+    return out
+
+
+# ----------------------------------------------------------------------------- projection GEMM
+def linear(a: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = None,
+           epilogue: str = "none") -> torch.Tensor:
+    """Row-independent a @ weight.T (bf16, fp32 accumulate): the bits of an output row depend only
+    on that row of `a`, never on how many rows the call has.
+      a: [m, k] with a contiguous last dim, or head-major [H, m, 128] (read in place as [m, H*128]);
+      weight: [n, k] (nn.Linear layout); epilogue "swiglu": weight = [gate; up] (2F rows) and the
+      result is silu(a @ gate.T) * (a @ up.T), [m, F]."""
+    _cuda(a, "a")
+    _cuda(weight, "weight")
+    if weight.dim() != 2 or weight.stride(-1) != 1:
+        raise H3Error("weight must be [out, in] with a contiguous last dim")
+    if a.dim() == 2:
+        if a.stride(-1) != 1:
+            raise H3Error("a must have a contiguous last dim")
+        m, k = a.shape
+        chunks, chunk_cols, chunk_stride, row_stride = 1, k, 0, a.stride(0)
+    elif a.dim() == 3:
+        if a.stride(-1) != 1:
+            raise H3Error("a must have a contiguous last dim")
+        chunks, m, chunk_cols = a.shape
+        chunk_stride, row_stride = a.stride(0), a.stride(1)
+        k = chunks * chunk_cols
+    else:
+        raise H3Error(f"a must be 2-D or 3-D, got {tuple(a.shape)}")
+    if weight.shape[1] != k:
+        raise H3Error(f"weight has {weight.shape[1]} inputs, a has {k}")
+    ep = {"none": 0, "swiglu": 1}.get(epilogue)
+    if ep is None:
+        raise H3Error(f"unknown epilogue {epilogue!r}")
+    n = weight.shape[0] // 2 if ep == 1 else weight.shape[0]
+    if ep == 1 and weight.shape[0] % 2:
+        raise H3Error("swiglu weight needs an even row count")
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=a.device)
+    else:
+        _cuda(out, "out")
+        if tuple(out.shape) != (m, n) or out.stride(-1) != 1:
+            raise H3Error(f"out must be [{m}, {n}] with a contiguous last dim")
+    rc = lib().h3_gemm_bf16(a.data_ptr(), m, chunks, chunk_cols, chunk_stride, row_stride, weight.data_ptr(), n,
+                            weight.stride(0), out.data_ptr(), out.stride(0), ep, status_word(a.device).data_ptr(),
+                            _stream())
+    _check(rc, "h3_gemm_bf16")
     return out
 
 

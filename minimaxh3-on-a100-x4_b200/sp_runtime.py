@@ -3,8 +3,8 @@
 Same module API and behaviour, B200 data path underneath:
 
   init()                       process group (NCCL) + device          (ref :60-65)
-  install(module=None)         patch MiniMaxH3Model.run_blocks and     (ref :258-271)
-                               Attention.forward of the host model module
+  install(module=None)         patch MiniMaxH3Model.run_blocks,        (ref :258-271)
+                               Attention.forward and MLP.forward of the host model module
   a2a_seq_to_head(x, world)    [1, H, Sl, d] -> [1, H/W, S, d]         (ref :67-71)
   a2a_head_to_seq(x, world, H) [1, H/W, S, d] -> [1, H, Sl, d]         (ref :73-77)
   get_timing()                 per-category ms of the last run_blocks  (ref :57-58)
@@ -16,6 +16,13 @@ What differs, by design:
     RMSNorm + RoPE and writes q, k, v straight into the all-to-all send buffer (one
     exchange for all three), the attention kernel reads the unpacked receive buffer and
     writes O straight into the head->seq send layout (or, at W=1, token-major for out_proj).
+  * The projections run on the library's row-independent GEMM (h3_gemm_bf16): qkv_proj,
+    out_proj (at W > 1 reading the head->seq receive buffer in place, no unpack pass) and,
+    through a patched MLP.forward (the reference's block-loop harness patches the same method,
+    harness/sp_blockloop.py:167-170), fc1 with the SwiGLU fused into its epilogue, then fc2.
+    An output row's bits do not depend on the shard it is computed in, so the whole layer and
+    block loop are bit-exact across W. A projection whose weight is not a bias-free bf16
+    matrix falls back to the host module's own op.
   * WORLD == 1 runs the same seam with this library's attention instead of falling through
     to the host model's own loop (ref :222-223), so W-way output is bit-exact against the
     1-GPU output of the same kernels.
@@ -47,6 +54,7 @@ _SP_ACTIVE = False
 _SP_REAL_S = None
 _orig_attn_forward = None
 _orig_run_blocks = None
+_orig_mlp_forward = None
 _MODULE = None
 
 _ops = None  # the kernel library binding (h3attn); resolved on first use
@@ -159,6 +167,27 @@ def _norm_inputs(self, x, rope_freqs):
     return rope, qw, kw
 
 
+def _gemm_weight(lin, x):
+    """The weight of a bias-free bf16 Linear that the projection GEMM takes for input x, or None
+    (then the host module's own op runs, as in the reference)."""
+    w = getattr(lin, "weight", None)
+    if not isinstance(w, torch.Tensor) or getattr(lin, "bias", None) is not None:
+        return None
+    if w.dtype != torch.bfloat16 or w.dim() != 2 or x.dtype != torch.bfloat16 or w.device != x.device:
+        return None
+    return w
+
+
+def _sp_mlp_forward(self, x):
+    """SwiGLU FFN (fc1 -> chunk(2) -> silu(gate) * up -> fc2) as two projection GEMMs, the
+    SwiGLU fused into fc1's epilogue (cf. harness/sp_blockloop.py:167-170)."""
+    w1, w2 = _gemm_weight(self.fc1, x), _gemm_weight(self.fc2, x)
+    if not _SP_ACTIVE or w1 is None or w2 is None or x.dim() != 2:
+        return _orig_mlp_forward(self, x)
+    O = ops()
+    return O.linear(O.linear(x, w1, epilogue="swiglu"), w2)
+
+
 def _sp_attn_forward(self, x, rope_freqs=None, transformer_options={}):
     if not _SP_ACTIVE:
         return _orig_attn_forward(self, x, rope_freqs=rope_freqs, transformer_options=transformer_options)
@@ -166,7 +195,9 @@ def _sp_attn_forward(self, x, rope_freqs=None, transformer_options={}):
     s = x.shape[0]
     H, D, W = self.heads, self.head_dim, WORLD
     with _tr("qkv"):
-        q, k, v = self.qkv_proj(x).split(H * D, dim=-1)
+        w_qkv = _gemm_weight(self.qkv_proj, x)
+        qkv = O.linear(x, w_qkv) if w_qkv is not None else self.qkv_proj(x)
+        q, k, v = qkv.split(H * D, dim=-1)
         rope, qw, kw = _norm_inputs(self, x, rope_freqs)
         send = O.qknorm_rope_pack(q, k, v, rope, qw, kw, self.q_norm.eps, W)  # [W, 3, H/W, s, D]
     with _tr("a2a_fwd"):
@@ -182,9 +213,13 @@ def _sp_attn_forward(self, x, rope_freqs=None, transformer_options={}):
         if W > 1:
             o_recv = _exchange(o_send)  # [W, H/W, s, D] == [H, s, D]
     with _tr("out_proj"):
+        w_out = _gemm_weight(self.out_proj, x)
         if W > 1:
-            o = O.head_to_seq_unpack(o_recv.view(H, s, D))
-        return self.out_proj(o)
+            o_heads = o_recv.view(H, s, D)
+            if w_out is not None:
+                return O.linear(o_heads, w_out)  # reads [H, s, D] as [s, H*D] in place
+            o = O.head_to_seq_unpack(o_heads)
+        return O.linear(o, w_out) if w_out is not None else self.out_proj(o)
 
 
 # ---- comm/compute overlap (exact): Q and O exchanged in token pieces on a side stream ----
@@ -215,7 +250,9 @@ def _sp_attn_forward_overlap(self, x, rope_freqs=None, transformer_options={}):
     O = ops()
     s = x.shape[0]
     H, D, W = self.heads, self.head_dim, WORLD
-    q, k, v = self.qkv_proj(x).split(H * D, dim=-1)
+    w_qkv = _gemm_weight(self.qkv_proj, x)
+    qkv = O.linear(x, w_qkv) if w_qkv is not None else self.qkv_proj(x)
+    q, k, v = qkv.split(H * D, dim=-1)
     rope, qw, kw = _norm_inputs(self, x, rope_freqs)
     send = O.qknorm_rope_pack(q, k, v, rope, qw, kw, self.q_norm.eps, W)  # [W, 3, H/W, s, D]
     kvh = O.seq_to_head_unpack(_exchange(send[:, 1:].contiguous()))  # K, V first (blocking)
@@ -245,7 +282,8 @@ def _sp_attn_forward_overlap(self, x, rope_freqs=None, transformer_options={}):
             o_send.record_stream(_comm_stream)
             O.head_to_seq_unpack(_exchange(o_send).view(H, hi - lo, D), out=o[lo:hi])
     default.wait_stream(_comm_stream)
-    return self.out_proj(o)
+    w_out = _gemm_weight(self.out_proj, x)
+    return O.linear(o, w_out) if w_out is not None else self.out_proj(o)
 
 
 def _shard_segments(segs, lo, hi):
@@ -320,7 +358,7 @@ def _sp_run_blocks(self, h, t_emb, mod_segments, rope_freqs, transformer_options
 
 def install(module=None):
     """Patch the host model module (default: ComfyUI's comfy.ldm.minimax.model)."""
-    global _orig_run_blocks, _orig_attn_forward, _MODULE
+    global _orig_run_blocks, _orig_attn_forward, _orig_mlp_forward, _MODULE
     if module is None:
         import comfy.ldm.minimax.model as module
     if _MODULE is not None and _MODULE is not module:
@@ -330,9 +368,13 @@ def install(module=None):
         _orig_run_blocks = module.MiniMaxH3Model.run_blocks
     if _orig_attn_forward is None:
         _orig_attn_forward = module.Attention.forward
+    if _orig_mlp_forward is None and hasattr(module, "MLP"):
+        _orig_mlp_forward = module.MLP.forward
     overlap = os.environ.get("SP_OVERLAP") == "1"
     module.Attention.forward = _sp_attn_forward_overlap if overlap else _sp_attn_forward
     module.MiniMaxH3Model.run_blocks = _sp_run_blocks
+    if _orig_mlp_forward is not None:
+        module.MLP.forward = _sp_mlp_forward
     if RANK == 0:
         mode = f"overlap(P={_PIECES})" if overlap else "blocking"
         print(f"[sp_runtime] installed (WORLD={WORLD}) - run_blocks + Ulysses attention patched [{mode}]"
@@ -340,11 +382,13 @@ def install(module=None):
 
 
 def uninstall():
-    """Restore the host module's original run_blocks / Attention.forward."""
-    global _orig_run_blocks, _orig_attn_forward, _MODULE
+    """Restore the host module's original run_blocks / Attention.forward / MLP.forward."""
+    global _orig_run_blocks, _orig_attn_forward, _orig_mlp_forward, _MODULE
     if _MODULE is not None:
         if _orig_run_blocks is not None:
             _MODULE.MiniMaxH3Model.run_blocks = _orig_run_blocks
         if _orig_attn_forward is not None:
             _MODULE.Attention.forward = _orig_attn_forward
-    _orig_run_blocks = _orig_attn_forward = _MODULE = None
+        if _orig_mlp_forward is not None:
+            _MODULE.MLP.forward = _orig_mlp_forward
+    _orig_run_blocks = _orig_attn_forward = _orig_mlp_forward = _MODULE = None

@@ -66,3 +66,18 @@ def head_to_seq_unpack(recv, out=None):
         out.copy_(res)
         return out
     return res
+
+
+def linear(a, weight, out=None, epilogue="none"):
+    """The projection GEMM as the host model computes it: nn.Linear without bias (a [m, k], or
+    head-major [H, m, 128] read as [m, H*128]); "swiglu": chunk(2) -> silu(gate) * up."""
+    if a.dim() == 3:
+        a = a.transpose(0, 1).reshape(a.shape[1], -1)
+    y = torch.nn.functional.linear(a, weight)
+    if epilogue == "swiglu":
+        g, u = y.chunk(2, dim=-1)
+        y = torch.nn.functional.silu(g) * u
+    if out is not None:
+        out.copy_(y)
+        return out
+    return y

@@ -80,6 +80,34 @@ def test_unpack_rejects_bad_arguments_before_launch(L):
     assert L.h3_status_read(None, None) == -1
 
 
+def test_gemm_rejects_bad_arguments_before_launch(L):
+    p, st = ctypes.c_void_p(0x1000), ctypes.c_void_p(0x2000)
+    # a [1][300][512], w [256][512], c [300][256]
+    ok = [p, 300, 1, 512, 0, 512, p, 256, 512, p, 256, 0, st, None]
+    bad = list(ok)
+    bad[6] = None
+    assert L.h3_gemm_bf16(*bad) == -1                    # NULL weight
+    bad = list(ok)
+    bad[9] = ctypes.c_void_p(0x1004)
+    assert L.h3_gemm_bf16(*bad) == -2                    # output not 16-byte aligned
+    bad = list(ok)
+    bad[7] = 100
+    assert L.h3_gemm_bf16(*bad) == -3                    # n_out not a multiple of 8
+    bad = list(ok)
+    bad[11] = 1
+    bad[7] = 192
+    assert L.h3_gemm_bf16(*bad) == -3                    # swiglu width not a multiple of 128
+    bad = list(ok)
+    bad[2], bad[3] = 4, 96
+    assert L.h3_gemm_bf16(*bad) == -3                    # chunked a needs 64-column chunks
+    bad = list(ok)
+    bad[8] = 256
+    assert L.h3_gemm_bf16(*bad) == -4                    # weight rows shorter than k
+    bad = list(ok)
+    bad[10] = 128
+    assert L.h3_gemm_bf16(*bad) == -4                    # output rows shorter than n_out
+
+
 def test_no_cpu_path():
     """The binding refuses host tensors instead of computing on the CPU."""
     import torch
