@@ -40,6 +40,7 @@ import torch.distributed as dist  # noqa: E402
 METRIC = "ms/layer & TFLOP/s, 56x128 attn S=42k bf16, 1/2/4/8 B200; % dense bf16 peak"
 UNIT = "TFLOP/s"
 HEADS, D = 56, 128
+NVLINK_GBS = 770.0  # measured peer copy per direction per GPU on this pool's B200s (nominal 900)
 
 
 def flops_layer(s: int, heads: int = HEADS) -> float:
@@ -208,15 +209,24 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     rope = h3_model.rope_freqs_1d(sl, pos0=rank * sl, device=dev)[0].contiguous()
     ones = torch.ones(D, dtype=torch.bfloat16, device=dev)
     eps = 1e-6
-    ev_att = []
+    ev_att, ev_a2a = [], []
+
+    def exchange(send, timed):
+        recv = torch.empty_like(send)
+        if timed:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+        dist.all_to_all_single(recv, send)
+        if timed:
+            b.record()
+            ev_a2a.append((a, b, send.numel() * send.element_size() * (W - 1) // W))
+        return recv
 
     def layer(x, out=None, timed=False):
         q, k, v = x.split(H * D, dim=-1)
         send = h3attn.qknorm_rope_pack(q, k, v, rope, ones, ones, eps, W)
         if W > 1:
-            recv = torch.empty_like(send)
-            dist.all_to_all_single(recv, send)
-            qkvh = h3attn.seq_to_head_unpack(recv)
+            qkvh = h3attn.seq_to_head_unpack(exchange(send, timed))
         else:
             qkvh = send[0]
         if timed:
@@ -230,8 +240,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
             e1.record()
             ev_att.append((e0, e1))
         if W > 1:
-            o_recv = torch.empty_like(o_send)
-            dist.all_to_all_single(o_recv, o_send)
+            o_recv = exchange(o_send, timed)
             o = h3attn.head_to_seq_unpack(o_recv.view(H, sl, D), out=out)
         return o
 
@@ -256,6 +265,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
 
     # ---- device-timed region
     ev_att.clear()
+    ev_a2a.clear()
     sync_all()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if sampler:
@@ -270,6 +280,9 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         sampler.stop()
     ms = max_over_ranks(t0.elapsed_time(t1) / args.steps)
     att_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in ev_att))
+    if W > 1:  # the blocking layer: both exchanges are exposed (nothing runs beside them)
+        a2a_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b, _ in ev_a2a) / args.steps)
+        a2a_bytes = sum(n for _, _, n in ev_a2a) / args.steps
     h3attn.check_status()
 
     # ---- end-to-end through the public API: every step copies its input from pinned host
@@ -339,6 +352,12 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         "gpu_launches": launches,
         "clocks": sampler.summary() if sampler else None,
     }
+    if W > 1:
+        gbs = a2a_bytes / (a2a_ms * 1e-3) / 1e9
+        line["a2a"] = {"exposed_ms_per_step": a2a_ms, "bytes_sent_per_gpu_per_step": a2a_bytes,
+                       "achieved_gbs_per_gpu": gbs, "frac_of_nvlink": gbs / NVLINK_GBS,
+                       "nvlink_ref": f"{NVLINK_GBS:.0f} GB/s per direction per GPU (measured peer copy on this pool)",
+                       "frac_of_step": a2a_ms / ms}
     if W == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
         heads, rows = 4, 4096
