@@ -160,6 +160,25 @@ int h3_gemm_bf16(const void* a, int64_t m, int64_t a_chunks, int64_t a_chunk_col
                  int64_t a_row_stride, const void* w, int64_t n_out, int64_t w_row_stride, void* c,
                  int64_t c_row_stride, int32_t epilogue, int32_t* status, void* stream);
 
+/* AdaLN modulation of the DiT block (the host model's norm + _mod_scale_shift, harness/sp_runtime.py:
+ * 209-210 and :214-215), optionally after its gated residual (_mod_gate, :212-213), in one pass:
+ *   xr = x + gate[seg] * y   (when y != NULL and the token is in a segment; else xr = x), stored to
+ *        x_out when x_out != NULL
+ *   h  = LN(xr) * (1 + scale[seg]) + shift[seg]   (LN(xr) alone for tokens outside every segment)
+ * LN is the affine-free LayerNorm (biased variance, eps), computed in fp32; every torch op of the
+ * host path rounds to bf16 and so does this kernel, in the same order. seg_row[token] is the
+ * modulation row of the token's segment or -1; gate / shift / scale are [rows][hidden] bf16 with
+ * row stride mod_row_stride. hidden <= 8192, a multiple of 8. */
+int h3_norm_modulate(const void* x, int64_t x_row_stride, const void* y, int64_t y_row_stride, const void* gate,
+                     void* x_out, int64_t x_out_row_stride, const void* shift, const void* scale,
+                     int64_t mod_row_stride, const int32_t* seg_row, void* h, int64_t h_row_stride, int64_t rows,
+                     int64_t hidden, float eps, void* stream);
+/* The block's closing gated residual (_mod_gate after the FFN, harness/sp_runtime.py:217-218):
+ * out = x + gate[seg] * y on segment tokens, x elsewhere (bf16 roundings as the host ops). */
+int h3_gated_residual(const void* x, int64_t x_row_stride, const void* y, int64_t y_row_stride, const void* gate,
+                      int64_t gate_row_stride, const int32_t* seg_row, void* out, int64_t out_row_stride,
+                      int64_t rows, int64_t hidden, void* stream);
+
 /* Tile known-answer tests of the tcgen05 path (cf. attn_sm80/microtest.py:10-26):
  *   h3_tile_kat_qk: s_out[128][128] fp32 = q[128][128] . k[128][128]^T
  *   h3_tile_kat_pv: o_out[128][128] fp32 = p[128][128] . v[128][128]  (p written to TMEM

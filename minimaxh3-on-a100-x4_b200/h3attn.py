@@ -76,6 +76,11 @@ def lib() -> ctypes.CDLL:
             getattr(L, name).restype = ctypes.c_int
         L.h3_gemm_bf16.argtypes = [vp, i64, i64, i64, i64, i64, vp, i64, i64, vp, i64, ctypes.c_int32, i32p, vp]
         L.h3_gemm_bf16.restype = ctypes.c_int
+        L.h3_norm_modulate.argtypes = [vp, i64, vp, i64, vp, vp, i64, vp, vp, i64, vp, vp, i64, i64, i64,
+                                       ctypes.c_float, vp]
+        L.h3_norm_modulate.restype = ctypes.c_int
+        L.h3_gated_residual.argtypes = [vp, i64, vp, i64, vp, i64, vp, vp, i64, i64, i64, vp]
+        L.h3_gated_residual.restype = ctypes.c_int
         L.h3_status_read.argtypes = [i32p, vp]
         L.h3_status_read.restype = ctypes.c_int
         _lib = L
@@ -301,6 +306,78 @@ def linear(a: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = Non
                             weight.stride(0), out.data_ptr(), out.stride(0), ep, status_word(a.device).data_ptr(),
                             _stream())
     _check(rc, "h3_gemm_bf16")
+    return out
+
+
+# ----------------------------------------------------------------------------- AdaLN modulation
+def segment_rows(mod_segments, rows: int, device) -> torch.Tensor:
+    """int32 [rows]: the modulation row of each token ((a, b, row) segments, later ones win as in
+    the host model's per-segment assignments), -1 outside every segment."""
+    seg = torch.full((rows,), -1, dtype=torch.int32, device=device)
+    for a, b, row in mod_segments:
+        a, b = max(int(a), 0), min(int(b), rows)
+        if a < b:
+            seg[a:b] = int(row)
+    return seg
+
+
+def _rows2d(t: torch.Tensor, name: str, hidden: int) -> None:
+    _cuda(t, name)
+    if t.dim() != 2 or t.shape[1] != hidden or t.stride(1) != 1:
+        raise H3Error(f"{name} must be [rows, {hidden}] with a contiguous last dim, got {tuple(t.shape)}")
+
+
+def norm_modulate(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, seg_row: torch.Tensor, eps: float,
+                  y: torch.Tensor | None = None, gate: torch.Tensor | None = None,
+                  x_out: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """h = LN(xr) * (1 + scale[seg]) + shift[seg] with xr = x + gate[seg] * y when y is given
+    (xr also written to x_out). x, y: [rows, hidden]; shift/scale/gate: [mod_rows, hidden] views
+    sharing one row stride; seg_row: int32 [rows]."""
+    rows, hidden = x.shape
+    _rows2d(x, "x", hidden)
+    for n, t in (("shift", shift), ("scale", scale)) + ((("gate", gate),) if y is not None else ()):
+        _rows2d(t, n, hidden)
+    if scale.stride(0) != shift.stride(0) or (y is not None and gate.stride(0) != shift.stride(0)):
+        raise H3Error("shift, scale and gate must share a row stride")
+    if y is not None:
+        _rows2d(y, "y", hidden)
+        if y.shape[0] != rows:
+            raise H3Error("y and x disagree on rows")
+    _cuda(seg_row, "seg_row", torch.int32)
+    if seg_row.shape != (rows,) or not seg_row.is_contiguous():
+        raise H3Error("seg_row must be a contiguous int32 [rows]")
+    if x_out is not None:
+        _rows2d(x_out, "x_out", hidden)
+    if out is None:
+        out = torch.empty((rows, hidden), dtype=torch.bfloat16, device=x.device)
+    else:
+        _rows2d(out, "out", hidden)
+    rc = lib().h3_norm_modulate(x.data_ptr(), x.stride(0), y.data_ptr() if y is not None else None,
+                                y.stride(0) if y is not None else 0, gate.data_ptr() if y is not None else None,
+                                x_out.data_ptr() if x_out is not None else None,
+                                x_out.stride(0) if x_out is not None else 0, shift.data_ptr(), scale.data_ptr(),
+                                shift.stride(0), seg_row.data_ptr(), out.data_ptr(), out.stride(0), rows, hidden,
+                                float(eps), _stream())
+    _check(rc, "h3_norm_modulate")
+    return out
+
+
+def gated_residual(x: torch.Tensor, y: torch.Tensor, gate: torch.Tensor, seg_row: torch.Tensor,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    """out = x + gate[seg] * y on segment tokens, x elsewhere."""
+    rows, hidden = x.shape
+    for n, t in (("x", x), ("y", y), ("gate", gate)):
+        _rows2d(t, n, hidden)
+    _cuda(seg_row, "seg_row", torch.int32)
+    if y.shape[0] != rows or seg_row.shape != (rows,) or not seg_row.is_contiguous():
+        raise H3Error("x, y and seg_row disagree on rows")
+    if out is None:
+        out = torch.empty((rows, hidden), dtype=torch.bfloat16, device=x.device)
+    else:
+        _rows2d(out, "out", hidden)
+    rc = lib().h3_gated_residual(x.data_ptr(), x.stride(0), y.data_ptr(), y.stride(0), gate.data_ptr(), gate.stride(0),
+                                 seg_row.data_ptr(), out.data_ptr(), out.stride(0), rows, hidden, _stream())
+    _check(rc, "h3_gated_residual")
     return out
 
 

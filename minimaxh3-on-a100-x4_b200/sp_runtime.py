@@ -23,6 +23,9 @@ What differs, by design:
     An output row's bits do not depend on the shard it is computed in, so the whole layer and
     block loop are bit-exact across W. A projection whose weight is not a bias-free bf16
     matrix falls back to the host module's own op.
+  * The block's AdaLN modulation and gated residuals run as three fused passes per block
+    (h3_norm_modulate, h3_gated_residual) when its norms are affine-free LayerNorms and the
+    activations are bf16 on the GPU; otherwise the host block runs.
   * WORLD == 1 runs the same seam with this library's attention instead of falling through
     to the host model's own loop (ref :222-223), so W-way output is bit-exact against the
     1-GPU output of the same kernels.
@@ -312,6 +315,37 @@ def _sp_block_timed(self, x, t_emb, mod_segments, rope_freqs, transformer_option
         return MM._mod_gate(x, gate_mlp, m, mod_segments)
 
 
+def _fusable(blk, x) -> bool:
+    """The block's norms are affine-free LayerNorms over the hidden width and x is bf16 on the GPU,
+    so the fused modulation kernels reproduce the host ops (else the host block runs)."""
+    if not (x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2 and x.shape[1] % 8 == 0 and x.shape[1] <= 8192):
+        return False
+    for n in (getattr(blk, "norm1", None), getattr(blk, "norm2", None)):
+        if not isinstance(n, torch.nn.LayerNorm) or n.weight is not None or n.bias is not None:
+            return False
+        if tuple(n.normalized_shape) != (x.shape[1],):
+            return False
+    return True
+
+
+def _sp_block(self, x, t_emb, seg_row, rope_freqs, transformer_options={}):
+    """The host block in the timed replica's op order (ref :203-218) with the AdaLN modulation and
+    gated residuals on the library's kernels, three passes over [rows, hidden]: norm1 + modulation;
+    attention residual + norm2 + modulation; FFN residual."""
+    O = ops()
+    with _tr("norm_mod"):
+        shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = self.adaln_proj(t_emb)
+        h = O.norm_modulate(x, shift_msa, scale_msa, seg_row, self.norm1.eps)
+    a = self.attn(h, rope_freqs=rope_freqs, transformer_options=transformer_options)
+    with _tr("residual"):
+        x1 = torch.empty_like(x)
+        h = O.norm_modulate(x, shift_mlp, scale_mlp, seg_row, self.norm2.eps, y=a, gate=gate_msa, x_out=x1)
+    with _tr("ffn"):
+        m = self.mlp(h)
+    with _tr("residual"):
+        return O.gated_residual(x1, m, gate_mlp, seg_row)
+
+
 def _gather_rows(h_loc: torch.Tensor) -> torch.Tensor:
     out = torch.empty((WORLD * h_loc.shape[0],) + tuple(h_loc.shape[1:]), dtype=h_loc.dtype, device=h_loc.device)
     if dist.get_backend() == "nccl":
@@ -341,9 +375,14 @@ def _sp_run_blocks(self, h, t_emb, mod_segments, rope_freqs, transformer_options
     blkfn = _sp_block_timed if _TIMING else None
     _SP_ACTIVE = True
     _SP_REAL_S = S
+    seg_row = None
     try:
         for blk in self.blocks:
-            if blkfn is not None:
+            if _fusable(blk, h_loc):
+                if seg_row is None:
+                    seg_row = ops().segment_rows(segs_loc, h_loc.shape[0], h_loc.device)
+                h_loc = _sp_block(blk, h_loc, t_emb, seg_row, rope_loc, transformer_options=transformer_options)
+            elif blkfn is not None:
                 h_loc = blkfn(blk, h_loc, t_emb, segs_loc, rope_loc, transformer_options=transformer_options)
             else:
                 h_loc = blk(h_loc, t_emb, segs_loc, rope_loc, transformer_options=transformer_options)
