@@ -829,6 +829,362 @@ __global__ void __launch_bounds__(kThreadsV2, 1)
   }
 }
 
+// ------------------------------------------------------------------ kernel v4: P through shared memory
+// The CTA shape of attn_fwd_kernel (two 128-row Q tiles, four softmax warps per tile, one query
+// row per thread), but P goes to shared memory -- one 16 KB SW128 buffer of 64 keys per Q tile,
+// reused by the two halves of a KV tile -- instead of S's TMEM columns. S_t is then free as soon
+// as the softmax has loaded it into registers, and the next S_t = Q_t K^T is issued right away,
+// under the softmax, instead of after P_t V: the per-tile chain shrinks to the softmax itself.
+// P*V reads P from shared memory (SS form). One MMA-issuing thread per Q tile (warps 1 and 3), so
+// one tile's hand-offs never wait behind the other's; K/V stages are released by both.
+constexpr int kStagesV4 = 4;
+constexpr uint32_t kOffQV4 = 0;
+constexpr uint32_t kOffPV4 = 2 * kTileBytes;                        // P_t: 16 KB each
+constexpr uint32_t kOffKVV4 = kOffPV4 + 2 * kHalfBytes;
+constexpr uint32_t kOffBarsV4 = kOffKVV4 + kStagesV4 * kTileBytes;  // 224 KB
+enum BarV4 : int {
+  kV4QFull = 0,
+  kV4KVFull = 1,
+  kV4KVEmpty = kV4KVFull + kStagesV4,  // released by both issuers
+  kV4SFull = kV4KVEmpty + kStagesV4,   // [t] S_t computed
+  kV4SFree = kV4SFull + 2,             // [t] S_t loaded into registers by the tile's 4 softmax warps
+  kV4PFullA = kV4SFree + 2,            // [t] P_t of keys 0..63 in shared memory
+  kV4PFullB = kV4PFullA + 2,           // [t] P_t of keys 64..127 in shared memory
+  kV4ODoneA = kV4PFullB + 2,           // [t] first-half P_t V retired (P buffer free again)
+  kV4ODone = kV4ODoneA + 2,            // [t] P_t V retired
+  kV4Drain = kV4ODone + 2,             // both issuers' MMAs retired
+  kV4Tok = kV4Drain + 1,               // [t] exp-phase token (kPingPong)
+  kV4NumBars = kV4Tok + 2
+};
+constexpr uint32_t kSmemBytesV4 = 1024 + kOffBarsV4 + kV4NumBars * 8 + 16;
+static_assert(kSmemBytesV4 <= 232448, "v4 shared memory exceeds the per-CTA limit");
+
+// O (+)= P V over 64 keys with P in shared memory: A = P (K-major, SW128, one 128-B row of 64
+// keys per query row, K steps +32 B), B = this half of V (MN-major) as in issue_pv_half.
+__device__ __forceinline__ void issue_pv_smem_half(uint32_t d_tmem, uint32_t p_base, uint32_t v_base, int half,
+                                                   bool accumulate) {
+  constexpr uint32_t idesc = idesc_bf16_f32(128, 128, 0, 1);
+  const uint64_t ad = smem_desc_sw128(p_base, 16, 1024);
+  const uint64_t bd = smem_desc_sw128(v_base + uint32_t(half) * 4u * 2048u, kHalfBytes, 1024);
+  const uint32_t alo = uint32_t(ad), ahi = uint32_t(ad >> 32), blo = uint32_t(bd), bhi = uint32_t(bd >> 32);
+#define H3_PVS_STEP(KK) \
+  "add.u32 la, %1, " #KK "*2;\n\t add.u32 lb, %3, " #KK "*128;\n\t" \
+  "mov.b64 da, {la, %2};\n\t mov.b64 db, {lb, %4};\n\t" \
+  "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %5, pt;\n\t"
+  asm volatile(
+      "{\n\t.reg .pred pf, pt;\n\t.reg .b32 la, lb;\n\t.reg .b64 da, db;\n\t"
+      "setp.ne.b32 pf, %6, 0;\n\t setp.eq.b32 pt, %6, %6;\n\t"
+      "mov.b64 da, {%1, %2};\n\t mov.b64 db, {%3, %4};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %5, pf;\n\t"
+      H3_PVS_STEP(1) H3_PVS_STEP(2) H3_PVS_STEP(3)
+      "}\n" ::"r"(d_tmem), "r"(alo), "r"(ahi), "r"(blo), "r"(bhi), "r"(idesc), "r"(accumulate ? 1u : 0u)
+      : "memory");
+#undef H3_PVS_STEP
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// kPingPong: the two tiles' softmax warpgroups take turns for each 64-key exp phase (a token
+// passed through two mbarriers: tile 0's n-th phase follows tile 1's (n-1)-th, tile 1's n-th
+// follows tile 0's n-th), so one exponentiates while the other loads, reduces and stores.
+template <bool kProf, bool kPingPong>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_fwd_v4_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
+                       const __grid_constant__ CUtensorMap tmap_v, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBarsV4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kV4NumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int head = blockIdx.y;
+  const int m0 = blockIdx.x * kRowsPerCta;
+  const int n_kv = p.n_kv_tiles;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(kV4QFull), 1);
+    for (int s = 0; s < kStagesV4; ++s) {
+      mbar_init(bar(kV4KVFull + s), 1);
+      mbar_init(bar(kV4KVEmpty + s), 2);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(bar(kV4SFull + t), 1);
+      mbar_init(bar(kV4SFree + t), 4);
+      mbar_init(bar(kV4PFullA + t), 4);
+      mbar_init(bar(kV4PFullB + t), 4);
+      mbar_init(bar(kV4ODoneA + t), 1);
+      mbar_init(bar(kV4ODone + t), 1);
+    }
+    mbar_init(bar(kV4Drain), 2);
+    mbar_init(bar(kV4Tok + 0), 4);
+    mbar_init(bar(kV4Tok + 1), 4);
+    *abort_flag = (*reinterpret_cast<volatile int*>(p.status) != 0) ? 1 : 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_q);
+    tma_prefetch_desc(&tmap_k);
+    tma_prefetch_desc(&tmap_v);
+  }
+  if (warp == 2) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const WaitCtx ctx{abort_flag, p.status};
+  const bool grid_aborted = *abort_flag != 0;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer: Q, then K_0, V_0, K_1, V_1, ...
+    if (lane == 0 && !grid_aborted) {
+      const uint32_t sq = sbase + kOffQV4;
+      const uint32_t skv = sbase + kOffKVV4;
+      mbar_expect_tx(bar(kV4QFull), 2 * kTileBytes);
+      for (int t = 0; t < 2; ++t)
+        for (int hh = 0; hh < 2; ++hh)
+          tma_load_3d(sq + t * kTileBytes + hh * kHalfBytes, &tmap_q, bar(kV4QFull), hh * 64, m0 + t * kBlockM, head);
+      int it = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        bool ok = true;
+        for (int kv = 0; kv < 2; ++kv, ++it) {
+          const int st = it % kStagesV4;
+          if (!mbar_wait(bar(kV4KVEmpty + st), (uint32_t(it / kStagesV4) & 1u) ^ 1u, ctx, kStatusTimeoutKV)) {
+            ok = false;
+            break;
+          }
+          const CUtensorMap* m = kv ? &tmap_v : &tmap_k;
+          mbar_expect_tx(bar(kV4KVFull + st), kTileBytes);
+          tma_load_3d(skv + st * kTileBytes, m, bar(kV4KVFull + st), 0, j * kBlockN, head);
+          tma_load_3d(skv + st * kTileBytes + kHalfBytes, m, bar(kV4KVFull + st), 64, j * kBlockN, head);
+        }
+        if (!ok) break;
+      }
+      drain_wait(bar(kV4QFull), 0, p.status);
+      for (int st = 0; st < kStagesV4; ++st) {
+        const int cnt = it / kStagesV4 + (st < it % kStagesV4 ? 1 : 0);
+        if (cnt > 0) drain_wait(bar(kV4KVFull + st), uint32_t(cnt - 1) & 1u, p.status);
+      }
+    }
+  } else if (warp == 1 || warp == 3) {
+    // ------------------------------------------------------------ MMA issuer of Q tile t
+    // Per iteration j: S_t(j+1) = Q_t K_{j+1}^T as soon as the softmax has taken S_t(j), then
+    // O_t += P_t V_j in two 64-key halves as the softmax hands them over.
+    if (lane == 0 && !grid_aborted) {
+      const int t = warp == 1 ? 0 : 1;
+      const uint32_t sq = sbase + kOffQV4 + t * kTileBytes;
+      const uint32_t sp = sbase + kOffPV4 + t * kHalfBytes;
+      const uint32_t skv = sbase + kOffKVV4;
+      const bool rec = t == 0 && blockIdx.x == 0 && blockIdx.y == 0;
+      auto wait_full = [&](int it) -> bool {
+        return mbar_wait(bar(kV4KVFull + it % kStagesV4), uint32_t(it / kStagesV4) & 1u, ctx, kStatusTimeoutKV);
+      };
+      bool ok = mbar_wait(bar(kV4QFull), 0, ctx, kStatusTimeoutQ) && wait_full(0);
+      if (ok) {
+        issue_qk(tmem + col_s(t), sq, skv);
+        mma_commit(bar(kV4SFull + t));
+        mma_commit(bar(kV4KVEmpty + 0));
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        prof_mark<kProf>(p, rec, 2, j, 0);
+        const uint32_t ph = uint32_t(j) & 1u;
+        const int it_v = 2 * j + 1, it_k = 2 * j + 2;
+        if (j + 1 < n_kv) {
+          if (!(ok = mbar_wait(bar(kV4SFree + t), ph, ctx, kStatusTimeoutP))) break;
+          prof_mark<kProf>(p, rec, 2, j, 1);
+          if (!(ok = wait_full(it_k))) break;
+          tc_fence_after();
+          issue_qk(tmem + col_s(t), sq, skv + (it_k % kStagesV4) * kTileBytes);
+          mma_commit(bar(kV4SFull + t));
+          mma_commit(bar(kV4KVEmpty + it_k % kStagesV4));
+          prof_mark<kProf>(p, rec, 2, j, 2);
+        }
+        if (!(ok = wait_full(it_v))) break;
+        const uint32_t sv = skv + (it_v % kStagesV4) * kTileBytes;
+        if (!(ok = mbar_wait(bar(kV4PFullA + t), ph, ctx, kStatusTimeoutP))) break;
+        prof_mark<kProf>(p, rec, 2, j, 3);
+        tc_fence_after();
+        issue_pv_smem_half(tmem + col_o(t), sp, sv, 0, j > 0);
+        mma_commit(bar(kV4ODoneA + t));
+        prof_mark<kProf>(p, rec, 2, j, 4);
+        if (!(ok = mbar_wait(bar(kV4PFullB + t), ph, ctx, kStatusTimeoutP))) break;
+        prof_mark<kProf>(p, rec, 2, j, 5);
+        tc_fence_after();
+        issue_pv_smem_half(tmem + col_o(t), sp, sv, 1, true);
+        mma_commit(bar(kV4ODone + t));
+        mma_commit(bar(kV4KVEmpty + it_v % kStagesV4));
+        prof_mark<kProf>(p, rec, 2, j, 6);
+      }
+      mma_commit(bar(kV4Drain));
+      drain_wait(bar(kV4Drain), 0, p.status);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ softmax + epilogue
+    const int t = (warp - 4) >> 2;  // Q tile
+    const int quad = warp & 3;      // TMEM lane quadrant this warp may access
+    const int r = quad * 32 + lane;  // row within the tile
+    const uint32_t lane_off = uint32_t(quad * 32) << 16;
+    const uint32_t tS = tmem + lane_off + col_s(t);
+    const uint32_t tO = tmem + lane_off + col_o(t);
+    const uint32_t p_row = sbase + kOffPV4 + t * kHalfBytes + uint32_t(r) * 128u;  // SW128: chunk c at c ^ (r & 7)
+    const uint32_t swz = uint32_t(r & 7);
+    const float c = p.scale_log2;
+    const int tail_valid = p.s_kv - (n_kv - 1) * kBlockN;
+    float m_run = -INFINITY;
+    float l_run = 0.f;
+    bool ok = !grid_aborted;
+    const bool rec = blockIdx.x == 0 && blockIdx.y == 0 && quad == 0 && lane == 0;
+
+    for (int j = 0; ok && j < n_kv; ++j) {
+      prof_mark<kProf>(p, rec, t, j, 0);
+      ok = __all_sync(0xffffffffu, mbar_wait(bar(kV4SFull + t), uint32_t(j) & 1u, ctx, kStatusTimeoutS));
+      if (!ok) break;
+      prof_mark<kProf>(p, rec, t, j, 1);
+      tc_fence_after();
+      uint32_t sa[64], sb[64];
+      tmem_ld64_wait(tS, sa);
+      tmem_ld64_wait(tS + 64, sb);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kV4SFree + t));  // S_t may be overwritten by the next Q_t K^T
+      float s[128];
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        s[i] = __uint_as_float(sa[i]);
+        s[64 + i] = __uint_as_float(sb[i]);
+      }
+      if (j == n_kv - 1 && tail_valid < kBlockN) {
+#pragma unroll
+        for (int i = 0; i < 128; ++i)
+          if (i >= tail_valid) s[i] = -INFINITY;
+      }
+      prof_mark<kProf>(p, rec, t, j, 2);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float mx0 = s[64 * h], mx1 = s[64 * h + 1], mx2 = s[64 * h + 2], mx3 = s[64 * h + 3];
+#pragma unroll
+        for (int i = 4; i < 64; i += 4) {
+          mx0 = fmaxf(mx0, s[64 * h + i]);
+          mx1 = fmaxf(mx1, s[64 * h + i + 1]);
+          mx2 = fmaxf(mx2, s[64 * h + i + 2]);
+          mx3 = fmaxf(mx3, s[64 * h + i + 3]);
+        }
+        const float m_new = fmaxf(m_run, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * c);
+        // The P*V this half must follow: h = 0 -> all of P(j-1) (o_done, phase j-1), which also
+        // frees the P buffer; h = 1 -> the first half of P(j) (o_done_a, phase j).
+        const uint32_t o_bar = bar(h == 0 ? kV4ODone + t : kV4ODoneA + t);
+        const uint32_t o_par = h == 0 ? uint32_t(j - 1) & 1u : uint32_t(j) & 1u;
+        const bool first = j == 0 && h == 0;
+        if (first) {
+          m_run = m_new;  // O is not written before P(0) V (accumulate off)
+        } else {
+          const bool need = m_new > m_run + kRescaleThreshold;
+          if (__any_sync(0xffffffffu, need)) {
+            if (!(ok = __all_sync(0xffffffffu, mbar_wait(o_bar, o_par, ctx, kStatusTimeoutO)))) break;
+            tc_fence_after();
+            const float f = need ? ex2_approx(m_run - m_new) : 1.0f;
+            if (need) {
+              l_run *= f;
+              m_run = m_new;
+            }
+#pragma unroll 1
+            for (int c16 = 0; c16 < 8; ++c16) {
+              uint32_t o[16];
+              tmem_ld16_wait(tO + c16 * 16, o);
+#pragma unroll
+              for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+              tmem_st16(tO + c16 * 16, o);
+            }
+            tmem_st_wait();
+          }
+        }
+        const int phase = 2 * j + h;  // this warpgroup's exp phase count
+        if (kPingPong && (t == 1 || phase > 0)) {
+          const uint32_t tp = t == 0 ? uint32_t(phase - 1) & 1u : uint32_t(phase) & 1u;
+          if (!(ok = __all_sync(0xffffffffu, mbar_wait(bar(kV4Tok + t), tp, ctx, kStatusTimeoutS)))) break;
+        }
+        const float neg_m = -m_run;
+        float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
+        uint32_t pk[32];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const int e = 64 * h + 2 * i;
+          const float e0 = ex2_approx(fmaf(s[e], c, neg_m));
+          const float e1 = ex2_approx(fmaf(s[e + 1], c, neg_m));
+          const float e2 = ex2_approx(fmaf(s[e + 2], c, neg_m));
+          const float e3 = ex2_approx(fmaf(s[e + 3], c, neg_m));
+          l0 += e0;
+          l1 += e1;
+          l2 += e2;
+          l3 += e3;
+          pk[i] = pack_bf16x2(e0, e1);
+          pk[i + 1] = pack_bf16x2(e2, e3);
+        }
+        if (kPingPong) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(kV4Tok + (t ^ 1)));  // hand the exp phase over
+        }
+        l_run += (l0 + l1) + (l2 + l3);
+        // the P buffer is free once the P*V that read it retired
+        if (!first && !(ok = __all_sync(0xffffffffu, mbar_wait(o_bar, o_par, ctx, kStatusTimeoutO)))) break;
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch)
+          st_shared_v4(p_row + ((uint32_t(ch) ^ swz) << 4), pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2],
+                       pk[4 * ch + 3]);
+        fence_proxy_async_smem();
+        tc_fence_before();  // the rescale's TMEM stores, if any, precede the hand-off too
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(h == 0 ? kV4PFullA + t : kV4PFullB + t));
+        prof_mark<kProf>(p, rec, t, j, 3 + h);
+      }
+    }
+    if (ok) {
+      ok = __all_sync(0xffffffffu, mbar_wait(bar(kV4ODone + t), uint32_t(n_kv - 1) & 1u, ctx, kStatusTimeoutO));
+    }
+    if (ok) {
+      tc_fence_after();
+      const float inv = 1.0f / l_run;
+      const int row = m0 + t * kBlockM + r;
+      const bool valid = row < p.s_q;
+      const long long rr = valid ? row : 0;
+      __nv_bfloat16* dst = p.o + (rr / p.o_rank_rows) * p.o_rank_stride + (long long)head * p.o_head_stride +
+                           (rr % p.o_rank_rows) * p.o_row_stride;
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t o[32];
+        tmem_ld32_wait(tO + c4 * 32, o);
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          w[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
+        if (valid) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + c4 * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 // ---------------------------------------------------------------- tile known-answer kernels
 // One 128x128x128 S = Q K^T through the same TMA / descriptor / tcgen05 path.
 __global__ void __launch_bounds__(128, 1)
@@ -1017,6 +1373,16 @@ static int launch_v2(dim3 grid, cudaStream_t st, const CUtensorMap& tq, const CU
   return cudaGetLastError() == cudaSuccess ? H3_OK : H3_ERR_LAUNCH;
 }
 
+template <bool kProf, bool kPingPong>
+static int launch_v4(dim3 grid, cudaStream_t st, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                     const Params& p) {
+  auto* kern = attn_fwd_v4_kernel<kProf, kPingPong>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytesV4) != cudaSuccess)
+    return H3_ERR_LAUNCH;
+  kern<<<grid, kThreads, kSmemBytesV4, st>>>(tq, tk, tv, p);
+  return cudaGetLastError() == cudaSuccess ? H3_OK : H3_ERR_LAUNCH;
+}
+
 constexpr int kDefaultVariant = 0;
 
 static int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, int64_t n_heads, int64_t s_q,
@@ -1079,6 +1445,8 @@ static int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, i
       case 8: return launch_v2<false, 4, true>(grid, st, tq, tk, tv, p);
       case 10: return launch_variant<false, 0, true, true>(grid, st, tq, tk, tv, p);
       case 11: return launch_variant<true, 0, true, true>(grid, st, tq, tk, tv, p);
+      case 16: return launch_v4<true, false>(grid, st, tq, tk, tv, p);
+      case 17: return launch_v4<true, true>(grid, st, tq, tk, tv, p);
       default: return H3_ERR_UNSUPPORTED;
     }
   }
@@ -1096,6 +1464,8 @@ static int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, i
     case 2: return launch_variant<true, 4>(grid, st, tq, tk, tv, p);
     case 3: return launch_variant<true, 8>(grid, st, tq, tk, tv, p);
     case 4: return launch_variant<true, 2>(grid, st, tq, tk, tv, p);
+    case 16: return launch_v4<false, false>(grid, st, tq, tk, tv, p);
+    case 17: return launch_v4<false, true>(grid, st, tq, tk, tv, p);
     default: return H3_ERR_UNSUPPORTED;
   }
 }
