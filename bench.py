@@ -190,7 +190,7 @@ def run_reference(args, rank: int, world: int) -> None:
 def config(args):
     return {"workload": "ulysses attention layer: qk-RMSNorm+RoPE pack, seq->head all-to-all, exact attention, "
                         "head->seq all-to-all", "heads": HEADS, "head_dim": D, "seq_len": args.seq, "batch": 1,
-            "parallelism": f"ulysses{args.gpus}",
+            "parallelism": f"ulysses{args.gpus}", "overlap": args.overlap if args.gpus > 1 else "none",
             "l2": f"inputs larger than L2: {args.seq * 3 * HEADS * D * 2 / 1e9:.2f} GB of QKV per step"}
 
 
@@ -243,6 +243,54 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
             o_recv = exchange(o_send, timed)
             o = h3attn.head_to_seq_unpack(o_recv.view(H, sl, D), out=out)
         return o
+
+    comm, side = (torch.cuda.Stream(), torch.cuda.Stream()) if W > 1 else (None, None)
+
+    def layer_heads(x, out=None, timed=False):
+        """The same layer pipelined head by head: each local head's q/k/v and O travel in their own
+        all-to-all on a side stream while other heads compute; consecutive heads alternate between
+        two compute streams so one head's tail wave overlaps the next head."""
+        q, k, v = x.split(H * D, dim=-1)
+        send = h3attn.qknorm_rope_pack(q, k, v, rope, ones, ones, eps, W, head_major=True)  # [hl, W, 3, sl, D]
+        default = torch.cuda.current_stream()
+        comm.wait_stream(default)
+        side.wait_stream(default)
+        send.record_stream(comm)
+        o_heads = torch.empty((W, hl, sl, D), dtype=torch.bfloat16, device=dev)
+        o_heads.record_stream(comm)
+        recvs, arrived = [], []
+        with torch.cuda.stream(comm):
+            for h in range(hl):
+                recvs.append(exchange(send[h], timed))
+                arrived.append(torch.cuda.Event())
+                arrived[-1].record(comm)
+        for h in range(hl):
+            cs = default if h % 2 == 0 else side
+            cs.wait_event(arrived[h])
+            recvs[h].record_stream(cs)
+            with torch.cuda.stream(cs):
+                qkvh = h3attn.seq_to_head_unpack(recvs[h].view(W, 3, 1, sl, D))
+                if timed:
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(cs)
+                o_send = h3attn.attention(qkvh[0], qkvh[1], qkvh[2], layout="send", world=W)
+                if timed:
+                    e1.record(cs)
+                    ev_att.append((e0, e1))
+                done = torch.cuda.Event()
+                done.record(cs)
+            o_send.record_stream(comm)
+            with torch.cuda.stream(comm):
+                comm.wait_event(done)
+                o_heads[:, h].copy_(exchange(o_send, timed).view(W, sl, D))
+        default.wait_stream(side)
+        default.wait_stream(comm)
+        return h3attn.head_to_seq_unpack(o_heads.view(H, sl, D), out=out)
+
+    heads_per_launch = hl
+    if W > 1 and args.overlap == "heads":
+        layer = layer_heads  # noqa: F811
+        heads_per_launch = 1
 
     def sync_all():
         torch.cuda.synchronize()
@@ -335,10 +383,13 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         return
     fl = flops_layer(S)
     burst, sustained, hbm, kind = peaks()
-    att_fl = 4.0 * S * S * D * hl  # one rank's launch
+    att_fl = 4.0 * S * S * D * heads_per_launch  # one attention launch
     achieved = att_fl / (att_ms * 1e-3) / 1e12
     traffic = profiled_traffic("attn_fwd_s8192_h56_full.md", S, hl)
-    launches = (2 if W == 1 else 4) * args.steps
+    # our kernels per step: pack, attention (W=1); + seq->head unpack and head->seq unpack (W>1),
+    # the unpack and attention once per local head when pipelined by heads
+    per_step = 2 if W == 1 else (4 if heads_per_launch == hl else 2 + 2 * hl)
+    launches = per_step * args.steps
     line = {
         "metric": METRIC, "value": fl / (ms * 1e-3) / 1e12, "unit": UNIT, "n_gpus": W, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
@@ -354,7 +405,8 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     }
     if W > 1:
         gbs = a2a_bytes / (a2a_ms * 1e-3) / 1e9
-        line["a2a"] = {"exposed_ms_per_step": a2a_ms, "bytes_sent_per_gpu_per_step": a2a_bytes,
+        key = "exposed_ms_per_step" if args.overlap == "none" else "comm_stream_ms_per_step_overlapped"
+        line["a2a"] = {key: a2a_ms, "bytes_sent_per_gpu_per_step": a2a_bytes,
                        "achieved_gbs_per_gpu": gbs, "frac_of_nvlink": gbs / NVLINK_GBS,
                        "nvlink_ref": f"{NVLINK_GBS:.0f} GB/s per direction per GPU (measured peer copy on this pool)",
                        "frac_of_step": a2a_ms / ms}
@@ -378,6 +430,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--seq", type=int, default=42000)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--overlap", default="none", choices=["none", "heads"],
+                    help="W>1: exchange and attention pipelined head by head")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))

@@ -180,10 +180,12 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, s_kv: int | Non
 # ----------------------------------------------------------------------------- pack / unpack
 def qknorm_rope_pack(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, rope: torch.Tensor | None,
                      q_weight: torch.Tensor | None, k_weight: torch.Tensor | None, eps: float, world: int,
-                     out: torch.Tensor | None = None) -> torch.Tensor:
+                     out: torch.Tensor | None = None, head_major: bool = False) -> torch.Tensor:
     """q, k, v: [S_l, H*128] (views of the fused QKV output are fine; rows may be strided).
     rope: fp32 [S_l, 64, 2, 2] or None. Returns the seq->head send buffer
-    [world, 3, H/world, S_l, 128] with q and k RMS-normalised (+ rotated)."""
+    [world, 3, H/world, S_l, 128] with q and k RMS-normalised (+ rotated); head_major=True lays
+    it out [H/world, world, 3, S_l, 128] instead, so each local head's blocks for all peers are
+    one contiguous all-to-all buffer (head-by-head pipelining)."""
     for n, t in (("q", q), ("k", k), ("v", v)):
         _cuda(t, n)
         if t.dim() == 3:
@@ -219,15 +221,19 @@ def qknorm_rope_pack(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, rope: to
         if tuple(w.shape) != (D,) or not w.is_contiguous():
             raise H3Error(f"{n} must be contiguous [128] bf16")
         wptr.append(w.data_ptr())
+    shape = (hl, world, 3, sl, D) if head_major else (world, 3, hl, sl, D)
     if out is None:
-        out = torch.empty((world, 3, hl, sl, D), dtype=torch.bfloat16, device=q.device)
-    elif tuple(out.shape) != (world, 3, hl, sl, D) or not out.is_contiguous():
-        raise H3Error("out must be contiguous [world, 3, heads/world, tokens, 128]")
-    tstride = hl * sl * D
+        out = torch.empty(shape, dtype=torch.bfloat16, device=q.device)
+    elif tuple(out.shape) != shape or not out.is_contiguous():
+        raise H3Error(f"out must be contiguous {shape}")
+    if head_major:  # element (h, rank, tensor, row) at ((h*world + rank)*3 + tensor)*sl + row
+        tstride, rank_stride, head_stride = sl * D, 3 * sl * D, world * 3 * sl * D
+    else:           # element (rank, tensor, h, row) at ((rank*3 + tensor)*hl + h)*sl + row
+        tstride, rank_stride, head_stride = hl * sl * D, 3 * hl * sl * D, sl * D
     base = out.data_ptr()
     rc = lib().h3_qknorm_rope_pack(q2.data_ptr(), k2.data_ptr(), v2.data_ptr(), q2.stride(0), rope_ptr, rope_stride,
                                    wptr[0], wptr[1], float(eps), base, base + 2 * tstride, base + 4 * tstride, sl, H,
-                                   hl, 3 * tstride, sl * D, _stream())
+                                   hl, rank_stride, head_stride, _stream())
     _check(rc, "h3_qknorm_rope_pack")
     return out
 

@@ -10,6 +10,7 @@ Same module API and behaviour, B200 data path underneath:
   get_timing()                 per-category ms of the last run_blocks  (ref :57-58)
   RANK, WORLD                  module constants from the environment   (ref :16-17)
   env SP_TIMING=1, SP_OVERLAP=1, SP_PIECES=N                           (ref :32, :133, :265)
+  env SP_OVERLAP=heads         head-by-head all-to-all / attention pipelining (this build)
 
 What differs, by design:
   * The attention layer runs on libh3attn.so (sm_100a): one fused kernel does the q/k
@@ -228,6 +229,7 @@ def _sp_attn_forward(self, x, rope_freqs=None, transformer_options={}):
 # ---- comm/compute overlap (exact): Q and O exchanged in token pieces on a side stream ----
 _PIECES = int(os.environ.get("SP_PIECES", "4"))
 _comm_stream = None
+_side_stream = None
 
 
 def _piece_bounds(n, p):
@@ -287,6 +289,68 @@ def _sp_attn_forward_overlap(self, x, rope_freqs=None, transformer_options={}):
     default.wait_stream(_comm_stream)
     w_out = _gemm_weight(self.out_proj, x)
     return O.linear(o, w_out) if w_out is not None else self.out_proj(o)
+
+
+def _sp_attn_forward_heads(self, x, rope_freqs=None, transformer_options={}):
+    """Same math, pipelined by heads (this build's SP_OVERLAP=heads; the reference pipelines token
+    pieces): the pack writes the send buffer head-major, each local head's q/k/v travels in its own
+    all-to-all on a side stream, and head h's attention and O exchange overlap the exchanges of the
+    heads after it. Consecutive heads alternate between two compute streams: one head's attention
+    grid is about one wave, so the next head fills the SMs its tail leaves idle. Heads are
+    independent, so the output is bit-identical to the blocking path."""
+    if not _SP_ACTIVE:
+        return _orig_attn_forward(self, x, rope_freqs=rope_freqs, transformer_options=transformer_options)
+    if WORLD == 1:
+        return _sp_attn_forward(self, x, rope_freqs=rope_freqs, transformer_options=transformer_options)
+    global _comm_stream, _side_stream
+    if _comm_stream is None:
+        _comm_stream = torch.cuda.Stream()
+    if _side_stream is None:
+        _side_stream = torch.cuda.Stream()
+    O = ops()
+    s = x.shape[0]
+    H, D, W = self.heads, self.head_dim, WORLD
+    hl = H // W
+    with _tr("qkv"):
+        w_qkv = _gemm_weight(self.qkv_proj, x)
+        qkv = O.linear(x, w_qkv) if w_qkv is not None else self.qkv_proj(x)
+        q, k, v = qkv.split(H * D, dim=-1)
+        rope, qw, kw = _norm_inputs(self, x, rope_freqs)
+        send = O.qknorm_rope_pack(q, k, v, rope, qw, kw, self.q_norm.eps, W, head_major=True)  # [hl, W, 3, s, D]
+    S_pad = W * s
+    s_kv = _SP_REAL_S if (_SP_REAL_S is not None and _SP_REAL_S < S_pad) else S_pad
+    default = torch.cuda.current_stream()
+    o_heads = torch.empty((W, hl, s, D), dtype=x.dtype, device=x.device)  # == [H, s, D], head g = src*hl + h
+    with _tr("fa2_local"):
+        _comm_stream.wait_stream(default)
+        _side_stream.wait_stream(default)
+        send.record_stream(_comm_stream)
+        o_heads.record_stream(_comm_stream)
+        recvs, arrived = [], []
+        with torch.cuda.stream(_comm_stream):
+            for h in range(hl):
+                recvs.append(_exchange(send[h]))  # [W(src), 3, s, D]
+                arrived.append(torch.cuda.Event())
+                arrived[-1].record(_comm_stream)
+        for h in range(hl):
+            cs = default if h % 2 == 0 else _side_stream
+            cs.wait_event(arrived[h])
+            recvs[h].record_stream(cs)
+            with torch.cuda.stream(cs):
+                qkvh = O.seq_to_head_unpack(recvs[h].view(W, 3, 1, s, D))  # [3, 1, W*s, D]
+                o_send = O.attention(qkvh[0], qkvh[1], qkvh[2], s_kv=s_kv, layout="send", world=W)  # [W, 1, s, D]
+                done = torch.cuda.Event()
+                done.record(cs)
+            o_send.record_stream(_comm_stream)
+            with torch.cuda.stream(_comm_stream):
+                _comm_stream.wait_event(done)
+                o_heads[:, h].copy_(_exchange(o_send).view(W, s, D))
+        default.wait_stream(_side_stream)
+        default.wait_stream(_comm_stream)
+    with _tr("out_proj"):
+        w_out = _gemm_weight(self.out_proj, x)
+        o_hsd = o_heads.view(H, s, D)
+        return O.linear(o_hsd, w_out) if w_out is not None else self.out_proj(O.head_to_seq_unpack(o_hsd))
 
 
 def _shard_segments(segs, lo, hi):
@@ -409,13 +473,15 @@ def install(module=None):
         _orig_attn_forward = module.Attention.forward
     if _orig_mlp_forward is None and hasattr(module, "MLP"):
         _orig_mlp_forward = module.MLP.forward
-    overlap = os.environ.get("SP_OVERLAP") == "1"
-    module.Attention.forward = _sp_attn_forward_overlap if overlap else _sp_attn_forward
+    mode = os.environ.get("SP_OVERLAP", "0")
+    overlap = mode == "1"
+    module.Attention.forward = {"1": _sp_attn_forward_overlap, "heads": _sp_attn_forward_heads}.get(
+        mode, _sp_attn_forward)
     module.MiniMaxH3Model.run_blocks = _sp_run_blocks
     if _orig_mlp_forward is not None:
         module.MLP.forward = _sp_mlp_forward
     if RANK == 0:
-        mode = f"overlap(P={_PIECES})" if overlap else "blocking"
+        mode = f"overlap(P={_PIECES})" if overlap else ("overlap(heads)" if mode == "heads" else "blocking")
         print(f"[sp_runtime] installed (WORLD={WORLD}) - run_blocks + Ulysses attention patched [{mode}]"
               + (" [SP_TIMING]" if _TIMING else ""), flush=True)
 

@@ -46,7 +46,7 @@ def _worker(rank, world, port, S, out_dir, overlap):
     os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port),
                       LOCAL_RANK=str(rank))
     if overlap:
-        os.environ["SP_OVERLAP"] = "1"
+        os.environ["SP_OVERLAP"] = overlap  # "1": token pieces, "heads": head by head
     import sp_runtime
     import h3attn
     sp_runtime.init(timeout_s=120)
@@ -71,13 +71,14 @@ def _worker(rank, world, port, S, out_dir, overlap):
             torch.distributed.destroy_process_group()
 
 
-def _run(world, S, out_dir, overlap=False):
+def _run(world, S, out_dir, overlap=None):
     import torch.multiprocessing as mp
     mp.start_processes(_worker, args=(world, _port(), S, str(out_dir), overlap), nprocs=world, start_method="spawn")
     return torch.load(os.path.join(out_dir, f"w{world}.pt"))
 
 
-@pytest.mark.parametrize("world,S,overlap", [(2, 1001, False), (2, 1024, True), (4, 1003, False), (8, 1000, False)])
+@pytest.mark.parametrize("world,S,overlap", [(2, 1001, None), (2, 1024, "1"), (2, 1001, "heads"), (4, 1003, "heads"),
+                                             (4, 1003, None), (8, 1000, None), (8, 1000, "heads")])
 def test_run_blocks_bit_exact_across_world(world, S, overlap, tmp_path):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
