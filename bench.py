@@ -189,9 +189,10 @@ def run_reference(args, rank: int, world: int) -> None:
 
 def config(args):
     return {"workload": "ulysses attention layer: qk-RMSNorm+RoPE pack, seq->head all-to-all, exact attention, "
-                        "head->seq all-to-all", "heads": HEADS, "head_dim": D, "seq_len": args.seq, "batch": 1,
-            "parallelism": f"ulysses{args.gpus}", "overlap": args.overlap if args.gpus > 1 else "none",
-            "l2": f"inputs larger than L2: {args.seq * 3 * HEADS * D * 2 / 1e9:.2f} GB of QKV per step"}
+                        "head->seq all-to-all", "heads": HEADS, "head_dim": D, "seq_len": args.seq,
+            "batch": args.batch, "parallelism": f"ulysses{args.gpus}",
+            "overlap": args.overlap if args.gpus > 1 else "none",
+            "l2": f"inputs larger than L2: {args.batch * args.seq * 3 * HEADS * D * 2 / 1e9:.2f} GB of QKV per step"}
 
 
 def run_ours(args, rank: int, world: int, local: int) -> None:
@@ -205,7 +206,9 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         raise SystemExit(f"seq {S} and heads {H} must divide by {W}")
     sl, hl = S // W, H // W
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
-    qkv = torch.randn((sl, 3 * H * D), generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    B = args.batch  # independent sequences per step (config 4: CFG cond/uncond, separate seeds)
+    qkv = torch.stack([torch.randn((sl, 3 * H * D), generator=torch.Generator(device=dev).manual_seed(1000 + rank + 7919 * b),
+                                   device=dev, dtype=torch.float32).to(torch.bfloat16) for b in range(B)])
     rope = h3_model.rope_freqs_1d(sl, pos0=rank * sl, device=dev)[0].contiguous()
     ones = torch.ones(D, dtype=torch.bfloat16, device=dev)
     eps = 1e-6
@@ -305,9 +308,17 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return t.item()
 
+    def step(x, out=None, timed=False):
+        """One step: the layer over each of the B sequences of x [B, Sl, 3*H*D]."""
+        if out is None:
+            out = torch.empty((B, sl, H * D), dtype=torch.bfloat16, device=dev)
+        for b in range(B):
+            layer(x[b], out=out[b], timed=timed)
+        return out
+
     # correctness guard: the status word must stay clean
     for _ in range(args.warmup):
-        layer(qkv)
+        step(qkv)
     h3attn.check_status()
     sync_all()
 
@@ -320,7 +331,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         sampler.mark_start()
     t0.record()
     for _ in range(args.steps):
-        layer(qkv, timed=True)
+        step(qkv, timed=True)
     t1.record()
     sync_all()
     if sampler:
@@ -338,9 +349,9 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     # buffers each way, so step i+1's upload and step i-1's readback overlap step i's layer.
     host_in = torch.empty(qkv.shape, dtype=qkv.dtype, pin_memory=True)
     host_in.copy_(qkv)
-    host_out = [torch.empty((sl, H * D), dtype=torch.bfloat16, pin_memory=True) for _ in range(2)]
+    host_out = [torch.empty((B, sl, H * D), dtype=torch.bfloat16, pin_memory=True) for _ in range(2)]
     dev_in = [torch.empty_like(qkv) for _ in range(2)]
-    dev_out = [torch.empty((sl, H * D), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    dev_out = [torch.empty((B, sl, H * D), dtype=torch.bfloat16, device=dev) for _ in range(2)]
     compute = torch.cuda.current_stream()
     s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
     ev = lambda: torch.cuda.Event()
@@ -358,7 +369,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
                 in_ready[b].record(s_in)
             compute.wait_event(in_ready[b])
             compute.wait_event(out_free[b])
-            layer(dev_in[b], out=dev_out[b])
+            step(dev_in[b], out=dev_out[b])
             in_free[b].record(compute)
             done[b].record(compute)
             with torch.cuda.stream(s_out):
@@ -376,12 +387,12 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     t1.record()
     sync_all()
     e2e_ms = max_over_ranks(t0.elapsed_time(t1) / e2e_n)
-    if not torch.equal(host_out[(e2e_n - 1) % 2], layer(qkv).cpu()):
+    if not torch.equal(host_out[(e2e_n - 1) % 2], step(qkv).cpu()):
         raise SystemExit("end-to-end output differs from the device-resident run")
 
     if rank != 0:
         return
-    fl = flops_layer(S)
+    fl = flops_layer(S) * B
     burst, sustained, hbm, kind = peaks()
     att_fl = 4.0 * S * S * D * heads_per_launch  # one attention launch
     achieved = att_fl / (att_ms * 1e-3) / 1e12
@@ -389,7 +400,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     # our kernels per step: pack, attention (W=1); + seq->head unpack and head->seq unpack (W>1),
     # the unpack and attention once per local head when pipelined by heads
     per_step = 2 if W == 1 else (4 if heads_per_launch == hl else 2 + 2 * hl)
-    launches = per_step * args.steps
+    launches = per_step * B * args.steps
     line = {
         "metric": METRIC, "value": fl / (ms * 1e-3) / 1e12, "unit": UNIT, "n_gpus": W, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
@@ -399,7 +410,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
                      "frac_of_burst_peak": achieved / burst, "traffic": traffic, "kernel": "attn_fwd_kernel",
                      "kernel_ms": att_ms, "flop_per_launch": att_fl},
         "e2e": {"value": fl / (e2e_ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": e2e_ms,
-                "h2d_bytes_per_step": qkv.numel() * 2 * W, "d2h_bytes_per_step": sl * H * D * 2 * W},
+                "h2d_bytes_per_step": qkv.numel() * 2 * W, "d2h_bytes_per_step": B * sl * H * D * 2 * W},
         "gpu_launches": launches,
         "clocks": sampler.summary() if sampler else None,
     }
@@ -430,6 +441,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--seq", type=int, default=42000)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=1, help="independent sequences per step (config 4: 2)")
     ap.add_argument("--overlap", default="none", choices=["none", "heads"],
                     help="W>1: exchange and attention pipelined head by head")
     args = ap.parse_args()
