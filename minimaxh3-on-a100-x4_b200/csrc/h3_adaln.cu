@@ -80,15 +80,18 @@ struct NormParams {
   float eps;
 };
 
-__global__ void __launch_bounds__(kThreads) norm_modulate_kernel(const NormParams p) {
+// kVec vectors of 8 per thread hold the row: 3 covers hidden <= 6144 (H3's 5376) and, with fewer
+// registers, lets six rows per SM be in flight instead of four; 4 covers the rest.
+template <int kVec>
+__global__ void __launch_bounds__(kThreads, kVec == 3 ? 6 : 4) norm_modulate_kernel(const NormParams p) {
   __shared__ float red[kThreads / 32 + 1];
   const long long r = blockIdx.x;
   const int m = p.seg_row[r];
   const int n_vec = p.hidden >> 3;
-  float v[kMaxVec][8];
+  float v[kVec][8];
   float s = 0.f;
 #pragma unroll
-  for (int i = 0; i < kMaxVec; ++i) {
+  for (int i = 0; i < kVec; ++i) {
     const int c = threadIdx.x + i * kThreads;
     if (c < n_vec) {
       unpack8(*reinterpret_cast<const uint4*>(p.x + r * p.x_stride + 8 * c), v[i]);
@@ -107,7 +110,7 @@ __global__ void __launch_bounds__(kThreads) norm_modulate_kernel(const NormParam
   const float mean = block_sum(s, red) / float(p.hidden);
   float q = 0.f;
 #pragma unroll
-  for (int i = 0; i < kMaxVec; ++i) {
+  for (int i = 0; i < kVec; ++i) {
     const int c = threadIdx.x + i * kThreads;
     if (c < n_vec) {
 #pragma unroll
@@ -119,7 +122,7 @@ __global__ void __launch_bounds__(kThreads) norm_modulate_kernel(const NormParam
   }
   const float rstd = rsqrtf(block_sum(q, red) / float(p.hidden) + p.eps);
 #pragma unroll
-  for (int i = 0; i < kMaxVec; ++i) {
+  for (int i = 0; i < kVec; ++i) {
     const int c = threadIdx.x + i * kThreads;
     if (c < n_vec) {
       float o[8];
@@ -200,7 +203,10 @@ extern "C" int h3_norm_modulate(const void* x, int64_t x_row_stride, const void*
   p.h_stride = h_row_stride;
   p.hidden = (int)hidden;
   p.eps = eps;
-  norm_modulate_kernel<<<(unsigned)rows, kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
+  if (hidden <= 8 * kThreads * 3)
+    norm_modulate_kernel<3><<<(unsigned)rows, kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
+  else
+    norm_modulate_kernel<kMaxVec><<<(unsigned)rows, kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
   return cudaGetLastError() == cudaSuccess ? H3_OK : H3_ERR_LAUNCH;
 }
 
