@@ -169,7 +169,8 @@ __device__ __forceinline__ float ex2_mixed(float x, int idx) {
 // kDual: one MMA-issuing thread per Q tile (warps 1 and 3) instead of one for both, so a
 // tile's P*V never waits behind the other tile's P hand-off; shared K/V stages are released
 // by both (arrival count 2) and each thread's commits track only its own MMAs.
-template <bool kPingPong, int kEmu, bool kProf, bool kDual = false>
+// kSpec: speculative exponentials (see the softmax loop).
+template <bool kPingPong, int kEmu, bool kProf, bool kDual = false, bool kSpec = false>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                     const __grid_constant__ CUtensorMap tmap_v, const Params p) {
@@ -430,45 +431,78 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        // every half holds at least one live key except possibly the second half of the last tile
-        float mx0 = s[64 * h], mx1 = s[64 * h + 1], mx2 = s[64 * h + 2], mx3 = s[64 * h + 3];
-#pragma unroll
-        for (int i = 4; i < 64; i += 4) {
-          mx0 = fmaxf(mx0, s[64 * h + i]);
-          mx1 = fmaxf(mx1, s[64 * h + i + 1]);
-          mx2 = fmaxf(mx2, s[64 * h + i + 2]);
-          mx3 = fmaxf(mx3, s[64 * h + i + 3]);
-        }
-        const float m_new = fmaxf(m_run, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * c);
-        if (j == 0 && h == 0) {
-          m_run = m_new;
-        } else if (h == 0) {
-          // S_t(j) ready implies every earlier P*V of this tile has retired
-          if (!(ok = rescale(m_new, 0, 0, true))) break;
-        } else {
-          if (!(ok = rescale(m_new, bar(kBarODoneA + t), uint32_t(j) & 1u, false))) break;
-        }
-        prof_mark<kProf>(p, rec, t, j, 3 + 2 * h);
-        const float neg_m = -m_run;
-        float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
+        float l0, l1, l2, l3;
         uint32_t pk[32];
+        // exponentials of this half against m_run (and, when asked, the half's raw max on the way).
+        // kSpec stores P to TMEM in two 16-column chunks as it goes (16 packed words live instead
+        // of 32); a redo overwrites them before the hand-off.
+        auto exps = [&](bool with_max, float& mx) {
+          const float neg_m = -m_run;
+          l0 = l1 = l2 = l3 = 0.f;
+          float x0 = s[64 * h], x1 = s[64 * h + 1];
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const int e = 64 * h + 2 * i;
-          const float e0 = ex2_mixed<kEmu>(fmaf(s[e], c, neg_m), e);
-          const float e1 = ex2_mixed<kEmu>(fmaf(s[e + 1], c, neg_m), e + 1);
-          const float e2 = ex2_mixed<kEmu>(fmaf(s[e + 2], c, neg_m), e + 2);
-          const float e3 = ex2_mixed<kEmu>(fmaf(s[e + 3], c, neg_m), e + 3);
-          l0 += e0;
-          l1 += e1;
-          l2 += e2;
-          l3 += e3;
-          pk[i] = pack_bf16x2(e0, e1);
-          pk[i + 1] = pack_bf16x2(e2, e3);
+          for (int i = 0; i < 32; i += 2) {
+            const int e = 64 * h + 2 * i;
+            if (with_max) {
+              x0 = fmaxf(x0, fmaxf(s[e], s[e + 2]));
+              x1 = fmaxf(x1, fmaxf(s[e + 1], s[e + 3]));
+            }
+            const float e0 = ex2_mixed<kEmu>(fmaf(s[e], c, neg_m), e);
+            const float e1 = ex2_mixed<kEmu>(fmaf(s[e + 1], c, neg_m), e + 1);
+            const float e2 = ex2_mixed<kEmu>(fmaf(s[e + 2], c, neg_m), e + 2);
+            const float e3 = ex2_mixed<kEmu>(fmaf(s[e + 3], c, neg_m), e + 3);
+            l0 += e0;
+            l1 += e1;
+            l2 += e2;
+            l3 += e3;
+            pk[i] = pack_bf16x2(e0, e1);
+            pk[i + 1] = pack_bf16x2(e2, e3);
+            if (kSpec && (i == 14 || i == 30)) {
+              uint32_t* chunk = pk + (i - 14);
+              tmem_st16(tP + 32 * h + (i - 14), *reinterpret_cast<uint32_t(*)[16]>(chunk));
+            }
+          }
+          mx = fmaxf(x0, x1);
+        };
+        // h = 0: S_t(j) ready implies every earlier P*V of this tile has retired; h = 1: O holds
+        // the first half of P_t(j) once o_done_a (phase j) completes
+        auto do_rescale = [&](float m_new) -> bool {
+          return h == 0 ? rescale(m_new, 0, 0, true) : rescale(m_new, bar(kBarODoneA + t), uint32_t(j) & 1u, false);
+        };
+        if (!kSpec || (j == 0 && h == 0)) {
+          // every half holds at least one live key except possibly the second half of the last tile
+          float mx0 = s[64 * h], mx1 = s[64 * h + 1], mx2 = s[64 * h + 2], mx3 = s[64 * h + 3];
+#pragma unroll
+          for (int i = 4; i < 64; i += 4) {
+            mx0 = fmaxf(mx0, s[64 * h + i]);
+            mx1 = fmaxf(mx1, s[64 * h + i + 1]);
+            mx2 = fmaxf(mx2, s[64 * h + i + 2]);
+            mx3 = fmaxf(mx3, s[64 * h + i + 3]);
+          }
+          const float m_new = fmaxf(m_run, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * c);
+          if (j == 0 && h == 0) {
+            m_run = m_new;
+          } else if (!(ok = do_rescale(m_new))) {
+            break;
+          }
+          prof_mark<kProf>(p, rec, t, j, 3 + 2 * h);
+          float unused;
+          exps(false, unused);
+        } else {
+          // kSpec: exponentiate against the running max first and take the half's max in the same
+          // pass; the rare half whose max jumps by more than 2^8 rescales and exponentiates again.
+          // Same decisions and values as the max-first order, off the softmax -> P*V chain.
+          float mx;
+          exps(true, mx);
+          const float m_new = fmaxf(m_run, mx * c);
+          const bool again = __any_sync(0xffffffffu, m_new > m_run + kRescaleThreshold);
+          if (!(ok = do_rescale(m_new))) break;
+          if (again) exps(false, mx);
+          prof_mark<kProf>(p, rec, t, j, 3 + 2 * h);
         }
         if (kPingPong && h == 1) mbar_arrive(bar(kBarTok + (t ^ 1)));  // hand the exp phase over
         l_run += (l0 + l1) + (l2 + l3);
-        tmem_st32(tP + 32 * h, pk);
+        if (!kSpec) tmem_st32(tP + 32 * h, pk);
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(bar(h == 0 ? kBarPFullA + t : kBarPFullB + t));
@@ -1353,10 +1387,10 @@ static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 using namespace h3::attn;
 
-template <bool kPingPong, int kEmu, bool kProf = false, bool kDual = false>
+template <bool kPingPong, int kEmu, bool kProf = false, bool kDual = false, bool kSpec = false>
 static int launch_variant(dim3 grid, cudaStream_t st, const CUtensorMap& tq, const CUtensorMap& tk,
                           const CUtensorMap& tv, const Params& p) {
-  auto* kern = attn_fwd_kernel<kPingPong, kEmu, kProf, kDual>;
+  auto* kern = attn_fwd_kernel<kPingPong, kEmu, kProf, kDual, kSpec>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) != cudaSuccess)
     return H3_ERR_LAUNCH;
   kern<<<grid, kThreads, kSmemBytes, st>>>(tq, tk, tv, p);
@@ -1447,6 +1481,7 @@ static int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, i
       case 11: return launch_variant<true, 0, true, true>(grid, st, tq, tk, tv, p);
       case 16: return launch_v4<true, false>(grid, st, tq, tk, tv, p);
       case 17: return launch_v4<true, true>(grid, st, tq, tk, tv, p);
+      case 18: return launch_variant<false, 0, true, false, true>(grid, st, tq, tk, tv, p);
       default: return H3_ERR_UNSUPPORTED;
     }
   }
@@ -1466,6 +1501,8 @@ static int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, i
     case 4: return launch_variant<true, 2>(grid, st, tq, tk, tv, p);
     case 16: return launch_v4<false, false>(grid, st, tq, tk, tv, p);
     case 17: return launch_v4<false, true>(grid, st, tq, tk, tv, p);
+    case 18: return launch_variant<false, 0, false, false, true>(grid, st, tq, tk, tv, p);
+    case 19: return launch_variant<false, 0, false, true, true>(grid, st, tq, tk, tv, p);
     default: return H3_ERR_UNSUPPORTED;
   }
 }
