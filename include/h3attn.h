@@ -94,6 +94,8 @@ int h3_attn_fwd(const void* q, const void* k, const void* v, void* o, int64_t n_
  *   18 as 0 with speculative exponentials: each half is exponentiated against the running max
  *      while its own max is taken, and redone in the rare case the max jumps (same results)
  *   19 as 18 with one MMA-issuing thread per Q tile (as 10)
+ *   20 as 0 on SM pairs: two-CTA clusters, every MMA a cta_group::2 pair MMA on the same Q tile of
+ *      both CTAs, each SM staging half of every K (by keys) and V (by head dimension) tile
  * Returns H3_ERR_UNSUPPORTED for any other value. */
 int h3_attn_fwd_variant(const void* q, const void* k, const void* v, void* o, int64_t n_heads, int64_t s_q,
                         int64_t s_kv, int64_t q_head_stride, int64_t q_row_stride, int64_t kv_head_stride,
@@ -101,7 +103,7 @@ int h3_attn_fwd_variant(const void* q, const void* k, const void* v, void* o, in
                         int64_t o_row_stride, float softmax_scale, int32_t* status, int32_t variant, void* stream);
 
 /* Phase profiler (diagnostics; cf. the clock64 phase counters of the reference kernel,
- * attn_sm80/fa3_sm80_h3.cu:96-105, :572-582): runs variants 0-3, 5, 6, 8, 10, 11, 13-17 or 18 and records clock64()
+ * attn_sm80/fa3_sm80_h3.cu:96-105, :572-582): runs variants 0-3, 5, 6, 8, 10, 11, 13-18 or 20 and records clock64()
  * stamps of CTA (0, 0) for the first trace_iters KV iterations into the device buffer
  *   trace[((role * trace_iters) + j) * 8 + point]   (int64, 3 * trace_iters * 8 entries)
  * role 0/1 = softmax warpgroup of Q tile 0/1: points 0 before the S wait, 1 S ready,

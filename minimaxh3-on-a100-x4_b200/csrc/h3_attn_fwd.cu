@@ -1440,7 +1440,7 @@ static int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, i
 
   const long long qhs = n_heads > 1 ? q_head_stride : s_q * q_row_stride;
   const long long kvhs = n_heads > 1 ? kv_head_stride : s_kv * kv_row_stride;
-  if (variant >= 13 && variant <= 15)
+  if ((variant >= 13 && variant <= 15) || variant == 20)
     return h3::pair::launch_attn(q, k, v, o, n_heads, s_q, s_kv, qhs, q_row_stride, kvhs, kv_row_stride, o_rank_rows,
                                  o_rank_stride, o_head_stride, o_row_stride,
                                  (float)((double)softmax_scale * 1.4426950408889634), status, variant, prof, prof_iters,

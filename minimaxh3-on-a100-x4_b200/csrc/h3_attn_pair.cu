@@ -3,7 +3,7 @@
 //   S = Q K^T: B = K split by keys (CTA r holds keys [64r, 64r+64) of the tile)
 //   O += P V : B = V split by head dimension (CTA r holds d in [64r, 64r+64))
 // This file holds the pair tile known-answer kernels (cf. attn_sm80/microtest.py:10-26) and the
-// SM-pair attention kernel (schedule variants 13-15 of h3_attn_fwd_variant).
+// SM-pair attention kernels (schedule variants 13-15 and 20 of h3_attn_fwd_variant).
 #include "h3_ptx.cuh"
 #include "h3attn.h"
 
@@ -888,6 +888,333 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kSoft > 0 ? kSplitTh
   }
 }
 
+// ---------------------------------------------------------------- SM pairs, two Q tiles per CTA
+// The schedule of the 1-SM kernel -- two 128-row Q tiles per CTA, one softmax warpgroup per tile
+// (one query row per thread), P written over columns [64,128) of S in TMEM, the next Q*K^T of a
+// tile issued after its P*V -- with every MMA a cta_group::2 pair MMA on tile t of both CTAs (256
+// rows): K split by keys, V split by head dimension, so each SM stages and reads only half of
+// every K and V tile (6 KB of shared-memory operands per Q*K^T MMA instead of 8 KB).
+constexpr int kP2Threads = 384;  // warp 0 TMA producer, warp 1 MMA (leader), warp 2 TMEM, warps 4..11 softmax
+constexpr int kP2Stages = 10;    // 16 KB half tiles: K (64 keys x 128 d) or V (128 keys x 64 d)
+constexpr uint32_t kP2OffQ = 0;
+constexpr uint32_t kP2OffRing = 2 * kQTileBytes;
+constexpr uint32_t kP2OffBars = kP2OffRing + kP2Stages * kStageBytes;
+enum P2Bar : int {
+  kP2QFull = 0,                       // leader: all four Q tiles of the pair landed
+  kP2KVFull = 1,                      // leader: both halves of a ring stage landed
+  kP2KVEmpty = kP2KVFull + kP2Stages, // both: stage consumed (multicast commit)
+  kP2SFull = kP2KVEmpty + kP2Stages,  // [t] both: S_t ready (multicast commit)
+  kP2PFullA = kP2SFull + 2,           // [t] leader: first 64 keys of P_t from the 8 softmax warps of both CTAs
+  kP2PFullB = kP2PFullA + 2,          // [t] leader: last 64 keys
+  kP2ODoneA = kP2PFullB + 2,          // [t] both: first-half P_t V retired
+  kP2ODone = kP2ODoneA + 2,           // [t] both: P_t V retired
+  kP2Drain = kP2ODone + 2,            // leader: every issued MMA retired
+  kP2NumBars = kP2Drain + 1
+};
+constexpr uint32_t kP2SmemBytes = 1024 + kP2OffBars + kP2NumBars * 8 + 16;
+static_assert(kP2SmemBytes <= 232448, "pair kernel shared memory exceeds the per-CTA limit");
+__host__ __device__ constexpr uint32_t p2_col_s(int t) { return uint32_t(t) * 128u; }
+__host__ __device__ constexpr uint32_t p2_col_p(int t) { return uint32_t(t) * 128u + 64u; }
+__host__ __device__ constexpr uint32_t p2_col_o(int t) { return 256u + uint32_t(t) * 128u; }
+
+template <bool kProf>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kP2Threads, 1)
+    attn_pair2_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
+                      const __grid_constant__ CUtensorMap tmap_v, const PairParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kP2OffBars);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kP2NumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int head = blockIdx.y;
+  const int m0 = (blockIdx.x >> 1) * 512 + 256 * int(rank);  // this CTA's rows: tile t = m0 + 128 t
+  const int n_kv = p.n_kv_tiles;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(kP2QFull), 1);
+    for (int s = 0; s < kP2Stages; ++s) {
+      mbar_init(bar(kP2KVFull + s), 1);
+      mbar_init(bar(kP2KVEmpty + s), 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(bar(kP2SFull + t), 1);
+      mbar_init(bar(kP2PFullA + t), 8);
+      mbar_init(bar(kP2PFullB + t), 8);
+      mbar_init(bar(kP2ODoneA + t), 1);
+      mbar_init(bar(kP2ODone + t), 1);
+    }
+    mbar_init(bar(kP2Drain), 1);
+    *abort_flag = (*reinterpret_cast<volatile int*>(p.status) != 0) ? 1 : 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_q);
+    tma_prefetch_desc(&tmap_k);
+    tma_prefetch_desc(&tmap_v);
+  }
+  if (warp == 2) {
+    tmem_alloc_pair(smem_u32(tmem_slot), 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers and TMEM of both CTAs exist before anything remote touches them
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const WaitCtx ctx{abort_flag, p.status};
+  const bool grid_aborted = *abort_flag != 0;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs): Q, K_0, V_0, K_1, ...
+    if (lane == 0 && !grid_aborted) {
+      const uint32_t sq = sbase + kP2OffQ;
+      const uint32_t ring = sbase + kP2OffRing;
+      if (rank == 0) mbar_expect_tx(bar(kP2QFull), 4 * kQTileBytes);
+      const uint32_t q_leader = mapa_shared(bar(kP2QFull), 0);
+      for (int t = 0; t < 2; ++t)
+        for (int hh = 0; hh < 2; ++hh)
+          tma_load_3d_pair(sq + t * kQTileBytes + hh * (kQTileBytes / 2), &tmap_q, q_leader, hh * 64, m0 + 128 * t,
+                           head);
+      int it = 0;
+      auto next_stage = [&](uint32_t& dst, uint32_t& full_leader) -> bool {
+        const int st = it % kP2Stages;
+        if (!mbar_wait(bar(kP2KVEmpty + st), (uint32_t(it / kP2Stages) & 1u) ^ 1u, ctx, kStatusTimeoutKV))
+          return false;
+        if (rank == 0) mbar_expect_tx(bar(kP2KVFull + st), 2 * kStageBytes);
+        dst = ring + st * kStageBytes;
+        full_leader = mapa_shared(bar(kP2KVFull + st), 0);
+        ++it;
+        return true;
+      };
+      auto load_k = [&](int kj) -> bool {
+        uint32_t dst, fb;
+        if (!next_stage(dst, fb)) return false;
+        for (int hh = 0; hh < 2; ++hh)
+          tma_load_3d_pair(dst + hh * (kHalfK / 2), &tmap_k, fb, hh * 64, kj * 128 + 64 * int(rank), head);
+        return true;
+      };
+      auto load_v = [&](int vj) -> bool {
+        uint32_t dst, fb;
+        if (!next_stage(dst, fb)) return false;
+        tma_load_3d_pair(dst, &tmap_v, fb, 64 * int(rank), vj * 128, head);
+        return true;
+      };
+      bool ok = load_k(0);
+      for (int j = 0; ok && j < n_kv; ++j) {
+        ok = load_v(j);
+        if (ok && j + 1 < n_kv) ok = load_k(j + 1);
+      }
+      if (rank == 0) {
+        // every copy of both CTAs counts on the leader's barriers: drain them before exit
+        drain_wait_pair(bar(kP2QFull), 0, p.status);
+        for (int st = 0; st < kP2Stages; ++st) {
+          const int cnt = it / kP2Stages + (st < it % kP2Stages ? 1 : 0);
+          if (cnt > 0) drain_wait_pair(bar(kP2KVFull + st), uint32_t(cnt - 1) & 1u, p.status);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader CTA)
+    if (rank == 0 && lane == 0 && !grid_aborted) {
+      const uint32_t sq = sbase + kP2OffQ;
+      const uint32_t ring = sbase + kP2OffRing;
+      const bool rec = blockIdx.x == 0 && blockIdx.y == 0;
+      int it = 0;
+      auto take = [&](uint32_t& base, int& st) -> bool {
+        st = it % kP2Stages;
+        const bool got =
+            mbar_wait_cluster(bar(kP2KVFull + st), uint32_t(it / kP2Stages) & 1u, ctx, kStatusTimeoutKV);
+        base = ring + st * kStageBytes;
+        ++it;
+        return got;
+      };
+      bool ok = mbar_wait_cluster(bar(kP2QFull), 0, ctx, kStatusTimeoutQ);
+      uint32_t kb = 0, vb = 0;
+      int stk = 0, stv = 0;
+      if (ok && (ok = take(kb, stk))) {
+        for (int t = 0; t < 2; ++t) {
+          issue_qk_pair(tmem + p2_col_s(t), sq + t * kQTileBytes, kb);
+          mma_commit_pair(bar(kP2SFull + t), 0x3);
+        }
+        mma_commit_pair(bar(kP2KVEmpty + stk), 0x3);
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        pmark<kProf>(p, rec, 2, j, 0);
+        const uint32_t ph = uint32_t(j) & 1u;
+        const bool next = j + 1 < n_kv;
+        if (!(ok = take(vb, stv))) break;
+        pmark<kProf>(p, rec, 2, j, 1);
+        for (int t = 0; t < 2; ++t) {
+          if (!(ok = mbar_wait_cluster(bar(kP2PFullA + t), ph, ctx, kStatusTimeoutP))) break;
+          pmark<kProf>(p, rec, 2, j, 2 + 3 * t);
+          tc_fence_after();
+          issue_pv_pair(tmem + p2_col_o(t), tmem + p2_col_p(t), vb, 0, j > 0);
+          mma_commit_pair(bar(kP2ODoneA + t), 0x3);
+          if (!(ok = mbar_wait_cluster(bar(kP2PFullB + t), ph, ctx, kStatusTimeoutP))) break;
+          pmark<kProf>(p, rec, 2, j, 3 + 3 * t);
+          tc_fence_after();
+          issue_pv_pair(tmem + p2_col_o(t), tmem + p2_col_p(t), vb, 1, true);
+          mma_commit_pair(bar(kP2ODone + t), 0x3);
+          if (t == 1) mma_commit_pair(bar(kP2KVEmpty + stv), 0x3);
+          if (next) {
+            if (t == 0 && !(ok = take(kb, stk))) break;  // overlaps the queued P*V work
+            issue_qk_pair(tmem + p2_col_s(t), sq + t * kQTileBytes, kb);  // S_t(j+1) after P_t(j) V
+            mma_commit_pair(bar(kP2SFull + t), 0x3);
+            if (t == 1) mma_commit_pair(bar(kP2KVEmpty + stk), 0x3);
+          }
+          pmark<kProf>(p, rec, 2, j, 4 + 3 * t);
+        }
+      }
+      mma_commit_pair(bar(kP2Drain), 0x1);
+      drain_wait_pair(bar(kP2Drain), 0, p.status);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ softmax + epilogue (both CTAs)
+    const int t = (warp - 4) >> 2;  // Q tile
+    const int quad = warp & 3;      // TMEM lane quadrant this warp may access
+    const uint32_t lane_off = uint32_t(quad * 32) << 16;
+    const uint32_t tS = tmem + lane_off + p2_col_s(t);
+    const uint32_t tP = tmem + lane_off + p2_col_p(t);
+    const uint32_t tO = tmem + lane_off + p2_col_o(t);
+    const float c = p.scale_log2;
+    const int tail_valid = p.s_kv - (n_kv - 1) * 128;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = !grid_aborted;
+    const bool rec = blockIdx.x == 0 && blockIdx.y == 0 && quad == 0 && lane == 0;
+
+    // Rescale O (and l) of the rows whose running max grew by more than 2^8; `o_ready` says
+    // whether every P*V accumulated so far has retired.
+    auto rescale = [&](float m_new, uint32_t o_bar, uint32_t o_parity, bool o_ready) -> bool {
+      const bool need = m_new > m_run + kPairRescaleThreshold;
+      if (!__any_sync(0xffffffffu, need)) return true;
+      if (!o_ready && !__all_sync(0xffffffffu, mbar_wait(o_bar, o_parity, ctx, kStatusTimeoutO))) return false;
+      tc_fence_after();
+      const float f = need ? ex2_approx(m_run - m_new) : 1.0f;
+      if (need) {
+        l_run *= f;
+        m_run = m_new;
+      }
+#pragma unroll 1
+      for (int c16 = 0; c16 < 8; ++c16) {
+        uint32_t o[16];
+        tmem_ld16_wait(tO + c16 * 16, o);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+        tmem_st16(tO + c16 * 16, o);
+      }
+      tmem_st_wait();
+      return true;
+    };
+
+    for (int j = 0; ok && j < n_kv; ++j) {
+      pmark<kProf>(p, rec, t, j, 0);
+      ok = __all_sync(0xffffffffu, mbar_wait(bar(kP2SFull + t), uint32_t(j) & 1u, ctx, kStatusTimeoutS));
+      if (!ok) break;
+      pmark<kProf>(p, rec, t, j, 1);
+      tc_fence_after();
+      uint32_t sa[64], sb[64];
+      tmem_ld64_wait(tS, sa);
+      tmem_ld64_wait(tS + 64, sb);
+      float s[128];
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        s[i] = __uint_as_float(sa[i]);
+        s[64 + i] = __uint_as_float(sb[i]);
+      }
+      if (j == n_kv - 1 && tail_valid < 128) {
+#pragma unroll
+        for (int i = 0; i < 128; ++i)
+          if (i >= tail_valid) s[i] = -INFINITY;
+      }
+      pmark<kProf>(p, rec, t, j, 2);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float mx0 = s[64 * h], mx1 = s[64 * h + 1], mx2 = s[64 * h + 2], mx3 = s[64 * h + 3];
+#pragma unroll
+        for (int i = 4; i < 64; i += 4) {
+          mx0 = fmaxf(mx0, s[64 * h + i]);
+          mx1 = fmaxf(mx1, s[64 * h + i + 1]);
+          mx2 = fmaxf(mx2, s[64 * h + i + 2]);
+          mx3 = fmaxf(mx3, s[64 * h + i + 3]);
+        }
+        const float m_new = fmaxf(m_run, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * c);
+        if (j == 0 && h == 0) {
+          m_run = m_new;
+        } else if (h == 0) {
+          // S_t(j) ready implies every earlier P_t V has retired (issued before it by the same thread)
+          if (!(ok = rescale(m_new, 0, 0, true))) break;
+        } else {
+          if (!(ok = rescale(m_new, bar(kP2ODoneA + t), uint32_t(j) & 1u, false))) break;
+        }
+        pmark<kProf>(p, rec, t, j, 3 + 2 * h);
+        const float neg_m = -m_run;
+        float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
+        uint32_t pk[32];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const int e = 64 * h + 2 * i;
+          const float e0 = ex2_approx(fmaf(s[e], c, neg_m));
+          const float e1 = ex2_approx(fmaf(s[e + 1], c, neg_m));
+          const float e2 = ex2_approx(fmaf(s[e + 2], c, neg_m));
+          const float e3 = ex2_approx(fmaf(s[e + 3], c, neg_m));
+          l0 += e0;
+          l1 += e1;
+          l2 += e2;
+          l3 += e3;
+          pk[i] = pack_bf16x2(e0, e1);
+          pk[i + 1] = pack_bf16x2(e2, e3);
+        }
+        l_run += (l0 + l1) + (l2 + l3);
+        tmem_st32(tP + 32 * h, pk);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(mapa_shared(bar((h == 0 ? kP2PFullA : kP2PFullB) + t), 0));
+        pmark<kProf>(p, rec, t, j, 4 + 2 * h);
+      }
+    }
+    if (ok) {
+      ok = __all_sync(0xffffffffu, mbar_wait(bar(kP2ODone + t), uint32_t(n_kv - 1) & 1u, ctx, kStatusTimeoutO));
+    }
+    if (ok) {
+      tc_fence_after();
+      const float inv = 1.0f / l_run;
+      const int row = m0 + 128 * t + quad * 32 + lane;
+      const bool valid = row < p.s_q;
+      const long long rr = valid ? row : 0;
+      __nv_bfloat16* dst = p.o + (rr / p.o_rank_rows) * p.o_rank_stride + (long long)head * p.o_head_stride +
+                           (rr % p.o_rank_rows) * p.o_row_stride;
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t o[32];
+        tmem_ld32_wait(tO + c4 * 32, o);
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          w[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
+        if (valid) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + c4 * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the leader's MMAs into this CTA's TMEM have retired; nothing remote is pending
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 512);
+  }
+}
+
 // ---------------------------------------------------------------- host
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -913,6 +1240,16 @@ int make_map(CUtensorMap* map, const void* base, long long rows, long long n_hea
 }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+template <bool kProf>
+static int launch_pair2(dim3 grid, cudaStream_t st, const CUtensorMap& tq, const CUtensorMap& tk,
+                        const CUtensorMap& tv, const PairParams& pp) {
+  auto* kern = attn_pair2_kernel<kProf>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kP2SmemBytes) != cudaSuccess)
+    return H3_ERR_LAUNCH;
+  kern<<<grid, kP2Threads, kP2SmemBytes, st>>>(tq, tk, tv, pp);
+  return cudaGetLastError() == cudaSuccess ? H3_OK : H3_ERR_LAUNCH;
+}
 
 template <bool kProf, int kSoft>
 static int launch_pair(dim3 grid, cudaStream_t st, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
@@ -947,6 +1284,10 @@ int launch_attn(const void* q, const void* k, const void* v, void* o, long long 
   pp.status = status;
   pp.prof = prof;
   pp.prof_iters = prof_iters;
+  if (variant == 20) {
+    dim3 grid2((unsigned)(2 * ((s_q + 511) / 512)), (unsigned)n_heads);
+    return prof != nullptr ? launch_pair2<true>(grid2, st, tq, tk, tv, pp) : launch_pair2<false>(grid2, st, tq, tk, tv, pp);
+  }
   dim3 grid((unsigned)(2 * ((s_q + 255) / 256)), (unsigned)n_heads);
   if (prof != nullptr) {
     if (variant == 13) return launch_pair<true, 0>(grid, st, tq, tk, tv, pp);

@@ -186,7 +186,7 @@ def test_bad_arguments_rejected(cuda_dev):
         h3attn.attention(q, q, q, layout="send", world=3)
 
 
-@pytest.mark.parametrize("variant", [0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15, 16, 17, 18, 19])
+@pytest.mark.parametrize("variant", [0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15, 16, 17, 18, 19, 20])
 def test_attention_variants_vs_oracle(cuda_dev, variant):
     """Every kernel schedule meets the tolerance; the ping-pong schedule without FMA-pipe
     exponentials is bit-identical to the free-running one (scheduling only)."""
@@ -213,7 +213,7 @@ def test_attention_variants_vs_oracle(cuda_dev, variant):
 
 @pytest.mark.parametrize("H,S", [(2, 1), (2, 100), (2, 128), (2, 129), (2, 256), (2, 257), (3, 300), (2, 513),
                                  (1, 1000)])
-@pytest.mark.parametrize("variant", [13, 14, 15, 16, 17, 18])
+@pytest.mark.parametrize("variant", [13, 14, 15, 16, 17, 18, 20])
 def test_pair_kernel_vs_oracle(cuda_dev, H, S, variant):
     """The SM-pair kernels (variants 13-15) and the P-in-shared-memory kernel (16) over ragged sizes: a pair whose second CTA has no rows
     (S <= 128 + 256k), a lone key tile, odd tails; rows past S are never written."""
