@@ -290,10 +290,48 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         default.wait_stream(comm)
         return h3attn.head_to_seq_unpack(o_heads.view(H, sl, D), out=out)
 
+    peer_bufs, peer_step = None, [0]
+    if W > 1 and args.overlap == "peer":
+        import sp_runtime
+        peer_bufs = sp_runtime._peer_buffers(sl, H, D, dev, slots=2)
+
+    def layer_peer(x, out=None, timed=False):
+        """The same layer with both exchanges fused into the kernels over NVLink peer memory: the
+        pack writes every head into its destination rank's attention input, the attention epilogue
+        writes every row into its destination rank's token-major output; a stream-ordered barrier
+        after each. Two buffer slots alternate so a step's readback never meets the next step's
+        peer writes. Returns this rank's [Sl, H*D] output (a symmetric buffer)."""
+        buf = peer_bufs[peer_step[0] % 2]
+        peer_step[0] += 1
+        q, k, v = x.split(H * D, dim=-1)
+        h3attn.qknorm_rope_pack_peer(q, k, v, rope, ones, ones, eps, W, buf["qkv_ptrs"], hl * S * D, S * D, rank * sl)
+        barrier(buf["flag"], timed)
+        qkvh = buf["qkv"]
+        if timed:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+        h3attn.attention_peer(qkvh[0], qkvh[1], qkvh[2], buf["o"], buf["o_ptrs"], sl, D, H * D)
+        if timed:
+            e1.record()
+            ev_att.append((e0, e1))
+        barrier(buf["flag"], timed)
+        return buf["o"]
+
+    def barrier(flag, timed):
+        if timed:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+        dist.all_reduce(flag)
+        if timed:
+            b.record()
+            ev_a2a.append((a, b, 0))
+
     heads_per_launch = hl
     if W > 1 and args.overlap == "heads":
         layer = layer_heads  # noqa: F811
         heads_per_launch = 1
+    if W > 1 and args.overlap == "peer":
+        layer = layer_peer  # noqa: F811
 
     def sync_all():
         torch.cuda.synchronize()
@@ -309,12 +347,9 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         return t.item()
 
     def step(x, out=None, timed=False):
-        """One step: the layer over each of the B sequences of x [B, Sl, 3*H*D]."""
-        if out is None:
-            out = torch.empty((B, sl, H * D), dtype=torch.bfloat16, device=dev)
-        for b in range(B):
-            layer(x[b], out=out[b], timed=timed)
-        return out
+        """One step: the layer over each of the B sequences of x [B, Sl, 3*H*D]; returns the B
+        outputs (views of `out` when given and the layer writes there)."""
+        return [layer(x[b], out=None if out is None else out[b], timed=timed) for b in range(B)]
 
     # correctness guard: the status word must stay clean
     for _ in range(args.warmup):
@@ -373,12 +408,13 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
                 t0.record(compute)
             compute.wait_event(in_ready[b])
             compute.wait_event(out_free[b])
-            step(dev_in[b], out=dev_out[b])
+            res = step(dev_in[b], out=None if peer_bufs is not None else dev_out[b])
             in_free[b].record(compute)
             done[b].record(compute)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(done[b])
-                host_out[b].copy_(dev_out[b], non_blocking=True)
+                for bb in range(B):
+                    host_out[b][bb].copy_(res[bb], non_blocking=True)
                 out_free[b].record(s_out)
         compute.wait_stream(s_in)
         compute.wait_stream(s_out)
@@ -392,7 +428,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     t1.record(compute)
     sync_all()
     e2e_ms = max_over_ranks(t0.elapsed_time(t1) / e2e_n)
-    if not torch.equal(host_out[(e2e_warm + e2e_n - 1) % 2], step(qkv).cpu()):
+    if not torch.equal(host_out[(e2e_warm + e2e_n - 1) % 2], torch.stack([r.cpu() for r in step(qkv)])):
         raise SystemExit("end-to-end output differs from the device-resident run")
 
     if rank != 0:
@@ -404,7 +440,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     traffic = profiled_traffic("attn_fwd_s8192_h56_full.md", S, hl)
     # our kernels per step: pack, attention (W=1); + seq->head unpack and head->seq unpack (W>1),
     # the unpack and attention once per local head when pipelined by heads
-    per_step = 2 if W == 1 else (4 if heads_per_launch == hl else 2 + 2 * hl)
+    per_step = 2 if W == 1 or peer_bufs is not None else (4 if heads_per_launch == hl else 2 + 2 * hl)
     launches = per_step * B * args.steps
     line = {
         "metric": METRIC, "value": fl / (ms * 1e-3) / 1e12, "unit": UNIT, "n_gpus": W, "steps": args.steps,
@@ -420,7 +456,13 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         "gpu_launches": launches,
         "clocks": sampler.summary() if sampler else None,
     }
-    if W > 1:
+    if W > 1 and peer_bufs is not None:
+        # the exchanges are stores of the pack and attention kernels; only the barriers stand alone
+        sent = B * 4 * sl * H * D * 2 * (W - 1) / W  # q, k, v and O rows bound for other ranks
+        line["a2a"] = {"barrier_ms_per_step": a2a_ms, "bytes_sent_per_gpu_per_step": sent,
+                       "mode": "fused into the pack and attention kernels (NVLink peer stores)",
+                       "frac_of_step": a2a_ms / ms}
+    elif W > 1:
         gbs = a2a_bytes / (a2a_ms * 1e-3) / 1e9
         key = "exposed_ms_per_step" if args.overlap == "none" else "comm_stream_ms_per_step_overlapped"
         line["a2a"] = {key: a2a_ms, "bytes_sent_per_gpu_per_step": a2a_bytes,
@@ -448,8 +490,8 @@ def main():
     ap.add_argument("--seq", type=int, default=42000)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=1, help="independent sequences per step (config 4: 2)")
-    ap.add_argument("--overlap", default="none", choices=["none", "heads"],
-                    help="W>1: exchange and attention pipelined head by head")
+    ap.add_argument("--overlap", default="none", choices=["none", "heads", "peer"],
+                    help="W>1: exchanges pipelined head by head, or fused into the kernels over peer memory")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))

@@ -150,6 +150,30 @@ int h3_seq_to_head_unpack(const void* recv, void* out, int64_t world, int64_t he
  * applied to the head->seq all-to-all receive buffer (:76-77). */
 int h3_head_to_seq_unpack(const void* recv, void* out, int64_t n_heads, int64_t s_l, void* stream);
 
+/* The two all-to-alls of the Ulysses layer fused into the kernels that produce their data, over
+ * NVLink peer memory (replacing a2a_seq_to_head + its receive permute, harness/sp_runtime.py:67-71,
+ * and a2a_head_to_seq + the head->seq transpose, :73-77 and :125). rank_base / o_peer are DEVICE
+ * arrays of W addresses, one per destination rank, each mapped into this process (e.g. symmetric
+ * memory); the caller orders the writes of all ranks before any read with a stream-ordered barrier.
+ *
+ * h3_qknorm_rope_pack_peer: as h3_qknorm_rope_pack, but head g of token t goes to rank
+ *   r = g / heads_per_rank at rank_base[r] + tensor*tensor_stride + (g % heads_per_rank)*head_stride
+ *   + (row_offset + t)*128 (elements): each rank's attention input [3][H/W][S][128] is written by all
+ *   ranks directly, no send buffer, exchange or unpack.
+ * h3_attn_fwd_peer: as h3_attn_fwd (default schedule), but query row i goes to rank
+ *   r = i / o_rank_rows at o_peer[r] + head*o_head_stride + (i % o_rank_rows)*o_row_stride, e.g. the
+ *   destination's token-major out_proj input [S/W][H*128] at this rank's column block. o_local is
+ *   this rank's own output buffer (argument checks only). Both kernels end with a system-scope
+ *   fence so their peer stores are visible to the barrier that follows. */
+int h3_qknorm_rope_pack_peer(const void* q, const void* k, const void* v, int64_t in_row_stride, const float* rope,
+                             int64_t rope_row_stride, const void* q_weight, const void* k_weight, float eps,
+                             const uint64_t* rank_base, int64_t tensor_stride, int64_t head_stride,
+                             int64_t row_offset, int64_t s_l, int64_t n_heads, int64_t heads_per_rank, void* stream);
+int h3_attn_fwd_peer(const void* q, const void* k, const void* v, void* o_local, const uint64_t* o_peer,
+                     int64_t n_heads, int64_t s_q, int64_t s_kv, int64_t q_head_stride, int64_t q_row_stride,
+                     int64_t kv_head_stride, int64_t kv_row_stride, int64_t o_rank_rows, int64_t o_head_stride,
+                     int64_t o_row_stride, float softmax_scale, int32_t* status, void* stream);
+
 /* Row-independent projection GEMM, bf16 in, fp32 accumulate, bf16 out:
  *   epilogue 0: c[m][n] = sum_k a[m][k] * w[n][k]                  (w has n_out rows)
  *   epilogue 1: c[m][n] = silu(a . w[n]) * (a . w[n_out + n])       (w = [gate; up], 2*n_out rows;

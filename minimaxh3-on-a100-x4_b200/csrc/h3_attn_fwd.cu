@@ -77,6 +77,9 @@ struct Params {
   int* status;
   long long* prof;  // phase timestamps of CTA (0, 0) when profiling, else nullptr
   int prof_iters;
+  // attn_fwd_kernel only: per destination rank, the base of that rank's output (a peer's memory
+  // over NVLink) replacing o + rank * o_rank_stride; nullptr otherwise
+  const unsigned long long* o_peer;
 };
 
 // Phase profiler (the counterpart of the reference kernel's clock64 counters): the first
@@ -519,8 +522,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row = m0 + t * kBlockM + quad * 32 + lane;
       const bool valid = row < p.s_q;
       const long long rr = valid ? row : 0;
-      __nv_bfloat16* dst = p.o + (rr / p.o_rank_rows) * p.o_rank_stride + (long long)head * p.o_head_stride +
-                           (rr % p.o_rank_rows) * p.o_row_stride;
+      __nv_bfloat16* obase = p.o_peer != nullptr
+                                 ? reinterpret_cast<__nv_bfloat16*>(p.o_peer[rr / p.o_rank_rows])
+                                 : p.o + (rr / p.o_rank_rows) * p.o_rank_stride;
+      __nv_bfloat16* dst = obase + (long long)head * p.o_head_stride + (rr % p.o_rank_rows) * p.o_row_stride;
 #pragma unroll
       for (int c4 = 0; c4 < 4; ++c4) {
         uint32_t o[32];
@@ -535,6 +540,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 4; ++i) d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
         }
       }
+      if (p.o_peer != nullptr) __threadfence_system();  // peer stores visible before the host-side barrier
     }
   }
 
@@ -1423,7 +1429,8 @@ static int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, i
                          int64_t s_kv, int64_t q_head_stride, int64_t q_row_stride, int64_t kv_head_stride,
                          int64_t kv_row_stride, int64_t o_rank_rows, int64_t o_rank_stride, int64_t o_head_stride,
                          int64_t o_row_stride, float softmax_scale, int32_t* status, int32_t variant,
-                         long long* prof, int prof_iters, void* stream) {
+                         long long* prof, int prof_iters, void* stream,
+                         const unsigned long long* o_peer = nullptr) {
   if (!q || !k || !v || !o || !status) return H3_ERR_NULL;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || (reinterpret_cast<uintptr_t>(status) & 3u))
     return H3_ERR_ALIGN;
@@ -1465,6 +1472,7 @@ static int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, i
   p.status = status;
   p.prof = prof;
   p.prof_iters = prof_iters;
+  p.o_peer = o_peer;
 
   dim3 grid((unsigned)((s_q + kRowsPerCta - 1) / kRowsPerCta), (unsigned)n_heads);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
@@ -1536,6 +1544,19 @@ extern "C" int h3_attn_fwd(const void* q, const void* k, const void* v, void* o,
   return h3_attn_fwd_variant(q, k, v, o, n_heads, s_q, s_kv, q_head_stride, q_row_stride, kv_head_stride,
                              kv_row_stride, o_rank_rows, o_rank_stride, o_head_stride, o_row_stride, softmax_scale,
                              status, kDefaultVariant, stream);
+}
+
+extern "C" int h3_attn_fwd_peer(const void* q, const void* k, const void* v, void* o_local, const uint64_t* o_peer,
+                                int64_t n_heads, int64_t s_q, int64_t s_kv, int64_t q_head_stride,
+                                int64_t q_row_stride, int64_t kv_head_stride, int64_t kv_row_stride,
+                                int64_t o_rank_rows, int64_t o_head_stride, int64_t o_row_stride, float softmax_scale,
+                                int32_t* status, void* stream) {
+  if (!o_peer) return H3_ERR_NULL;
+  if (reinterpret_cast<uintptr_t>(o_peer) & 7u) return H3_ERR_ALIGN;
+  if (kDefaultVariant != 0) return H3_ERR_UNSUPPORTED;  // the peer epilogue lives in attn_fwd_kernel
+  return attn_fwd_impl(q, k, v, o_local, n_heads, s_q, s_kv, q_head_stride, q_row_stride, kv_head_stride,
+                       kv_row_stride, o_rank_rows, 0, o_head_stride, o_row_stride, softmax_scale, status,
+                       kDefaultVariant, nullptr, 0, stream, reinterpret_cast<const unsigned long long*>(o_peer));
 }
 
 extern "C" int h3_tile_kat_qk(const void* q, const void* k, float* s_out, int32_t* status, void* stream) {

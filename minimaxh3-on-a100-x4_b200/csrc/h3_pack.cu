@@ -74,7 +74,8 @@ __global__ void __launch_bounds__(256, 2) qknorm_rope_pack_kernel(
     long long in_row_stride, const float* __restrict__ rope, long long rope_row_stride,
     const __nv_bfloat16* __restrict__ qw, const __nv_bfloat16* __restrict__ kw, float eps,
     __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ k_out, __nv_bfloat16* __restrict__ v_out,
-    long long s_l, int n_heads, int heads_per_rank, long long out_rank_stride, long long out_head_stride) {
+    long long s_l, int n_heads, int heads_per_rank, long long out_rank_stride, long long out_head_stride,
+    const unsigned long long* __restrict__ rank_base, long long tensor_stride, long long row_offset) {
   const int lane = threadIdx.x & 31;
   const int g = lane & 7;
   const int grp = lane >> 3;
@@ -123,15 +124,22 @@ __global__ void __launch_bounds__(256, 2) qknorm_rope_pack_kernel(
           o1 = u[pr][1];
         }
         if (r < n_rows) {
-          __nv_bfloat16* dst = (tensor == 0 ? q_out : (tensor == 1 ? k_out : v_out)) +
-                               (long long)(h / heads_per_rank) * out_rank_stride +
-                               (long long)(h % heads_per_rank) * out_head_stride + tok * kD;
+          // rank_base: the destination rank's buffer (a peer's memory over NVLink), laid out
+          // [tensor][head][row]; otherwise one local send buffer addressed by rank / head strides
+          __nv_bfloat16* dst =
+              rank_base != nullptr
+                  ? reinterpret_cast<__nv_bfloat16*>(rank_base[h / heads_per_rank]) + tensor * tensor_stride +
+                        (long long)(h % heads_per_rank) * out_head_stride + (row_offset + tok) * kD
+                  : (tensor == 0 ? q_out : (tensor == 1 ? k_out : v_out)) +
+                        (long long)(h / heads_per_rank) * out_rank_stride +
+                        (long long)(h % heads_per_rank) * out_head_stride + tok * kD;
           reinterpret_cast<uint4*>(dst + 8 * g)[0] = o0;
           reinterpret_cast<uint4*>(dst + 64 + 8 * g)[0] = o1;
         }
       }
     }
   }
+  if (rank_base != nullptr) __threadfence_system();  // peer stores visible before the host-side barrier
 }
 
 // Chunk (r, t, h) of s_l*128 contiguous elements moves to out_t[h][r*s_l ...]: grid.y
@@ -209,7 +217,33 @@ extern "C" int h3_qknorm_rope_pack(const void* q, const void* k, const void* v, 
       reinterpret_cast<const __nv_bfloat16*>(q_weight), reinterpret_cast<const __nv_bfloat16*>(k_weight), eps,
       reinterpret_cast<__nv_bfloat16*>(q_out), reinterpret_cast<__nv_bfloat16*>(k_out),
       reinterpret_cast<__nv_bfloat16*>(v_out), s_l, (int)n_heads, (int)heads_per_rank, out_rank_stride,
-      out_head_stride);
+      out_head_stride, nullptr, 0, 0);
+  return cudaGetLastError() == cudaSuccess ? H3_OK : H3_ERR_LAUNCH;
+}
+
+extern "C" int h3_qknorm_rope_pack_peer(const void* q, const void* k, const void* v, int64_t in_row_stride,
+                                        const float* rope, int64_t rope_row_stride, const void* q_weight,
+                                        const void* k_weight, float eps, const uint64_t* rank_base,
+                                        int64_t tensor_stride, int64_t head_stride, int64_t row_offset, int64_t s_l,
+                                        int64_t n_heads, int64_t heads_per_rank, void* stream) {
+  if (!q || !k || !v || !rank_base) return H3_ERR_NULL;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || (rope && !aligned16(rope)) ||
+      (q_weight && !aligned16(q_weight)) || (k_weight && !aligned16(k_weight)) ||
+      (reinterpret_cast<uintptr_t>(rank_base) & 7u))
+    return H3_ERR_ALIGN;
+  if (s_l < 1 || n_heads < 1 || heads_per_rank < 1 || n_heads % heads_per_rank || row_offset < 0) return H3_ERR_SHAPE;
+  if (s_l * 3 * n_heads > (1ll << 40)) return H3_ERR_SHAPE;
+  if (in_row_stride < n_heads * 128 || (in_row_stride % 8) || (tensor_stride % 8) || (head_stride % 8) ||
+      tensor_stride < 0 || head_stride < 0 || (rope && (rope_row_stride < 256 || (rope_row_stride % 4))))
+    return H3_ERR_STRIDE;
+  if (!(eps >= 0.f)) return H3_ERR_SHAPE;
+  const int blocks = grid_for(s_l, 8, 148 * 8);
+  qknorm_rope_pack_kernel<<<(unsigned)blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const __nv_bfloat16*>(q), reinterpret_cast<const __nv_bfloat16*>(k),
+      reinterpret_cast<const __nv_bfloat16*>(v), in_row_stride, rope, rope_row_stride,
+      reinterpret_cast<const __nv_bfloat16*>(q_weight), reinterpret_cast<const __nv_bfloat16*>(k_weight), eps,
+      nullptr, nullptr, nullptr, s_l, (int)n_heads, (int)heads_per_rank, 0, head_stride,
+      reinterpret_cast<const unsigned long long*>(rank_base), tensor_stride, row_offset);
   return cudaGetLastError() == cudaSuccess ? H3_OK : H3_ERR_LAUNCH;
 }
 

@@ -81,6 +81,11 @@ def lib() -> ctypes.CDLL:
         L.h3_norm_modulate.restype = ctypes.c_int
         L.h3_gated_residual.argtypes = [vp, i64, vp, i64, vp, i64, vp, vp, i64, i64, i64, vp]
         L.h3_gated_residual.restype = ctypes.c_int
+        L.h3_qknorm_rope_pack_peer.argtypes = [vp, vp, vp, i64, vp, i64, vp, vp, ctypes.c_float, vp, i64, i64, i64,
+                                               i64, i64, i64, vp]
+        L.h3_qknorm_rope_pack_peer.restype = ctypes.c_int
+        L.h3_attn_fwd_peer.argtypes = [vp] * 5 + [i64] * 10 + [ctypes.c_float, i32p, vp]
+        L.h3_attn_fwd_peer.restype = ctypes.c_int
         L.h3_status_read.argtypes = [i32p, vp]
         L.h3_status_read.restype = ctypes.c_int
         _lib = L
@@ -177,15 +182,53 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, s_kv: int | Non
     return out
 
 
+# ----------------------------------------------------------------------------- fused exchanges (peer memory)
+def qknorm_rope_pack_peer(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, rope: torch.Tensor | None,
+                          q_weight: torch.Tensor | None, k_weight: torch.Tensor | None, eps: float, world: int,
+                          rank_base: torch.Tensor, tensor_stride: int, head_stride: int, row_offset: int) -> None:
+    """The pack with the seq->head exchange fused in: head g of each token goes straight to rank
+    g // (H/world)'s buffer at rank_base[rank] (int64 device tensor [world] of addresses mapped in
+    this process) + tensor*tensor_stride + local_head*head_stride + (row_offset + token)*128."""
+    q2, k2, v2, sl, H, rope_ptr, rope_stride, wptr = _pack_args(q, k, v, rope, q_weight, k_weight)
+    if H % world:
+        raise H3Error(f"heads {H} not divisible by world {world}")
+    _cuda(rank_base, "rank_base", torch.int64)
+    if tuple(rank_base.shape) != (world,) or not rank_base.is_contiguous():
+        raise H3Error("rank_base must be a contiguous int64 [world] device tensor")
+    rc = lib().h3_qknorm_rope_pack_peer(q2.data_ptr(), k2.data_ptr(), v2.data_ptr(), q2.stride(0), rope_ptr,
+                                        rope_stride, wptr[0], wptr[1], float(eps), rank_base.data_ptr(),
+                                        tensor_stride, head_stride, row_offset, sl, H, H // world, _stream())
+    _check(rc, "h3_qknorm_rope_pack_peer")
+
+
+def attention_peer(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o_local: torch.Tensor, o_peer: torch.Tensor,
+                   rank_rows: int, head_stride: int, row_stride: int, s_kv: int | None = None,
+                   scale: float | None = None) -> None:
+    """Attention with the head->seq exchange fused into the epilogue: query row i of head h goes to
+    o_peer[i // rank_rows] + h*head_stride + (i % rank_rows)*row_stride (elements)."""
+    for n, t in (("q", q), ("k", k), ("v", v)):
+        _cuda(t, n)
+        if t.dim() != 3 or t.shape[-1] != D or t.stride(-1) != 1:
+            raise H3Error(f"{n} must be [heads, rows, 128] with a contiguous last dim")
+    _cuda(o_local, "o_local")
+    _cuda(o_peer, "o_peer", torch.int64)
+    H, sq, _ = q.shape
+    if k.shape[0] != H or v.shape[0] != H or k.shape[1] != v.shape[1] or k.stride() != v.stride():
+        raise H3Error("q, k, v disagree on heads, key count or strides")
+    if o_peer.dim() != 1 or o_peer.shape[0] * rank_rows < sq or not o_peer.is_contiguous():
+        raise H3Error("o_peer must hold one address per destination rank")
+    s_kv = k.shape[1] if s_kv is None else int(s_kv)
+    scale = 1.0 / math.sqrt(D) if scale is None else float(scale)
+    rc = lib().h3_attn_fwd_peer(q.data_ptr(), k.data_ptr(), v.data_ptr(), o_local.data_ptr(), o_peer.data_ptr(), H,
+                                sq, s_kv, q.stride(0), q.stride(1), k.stride(0), k.stride(1), rank_rows, head_stride,
+                                row_stride, scale, status_word(q.device).data_ptr(), _stream())
+    _check(rc, "h3_attn_fwd_peer")
+
+
 # ----------------------------------------------------------------------------- pack / unpack
-def qknorm_rope_pack(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, rope: torch.Tensor | None,
-                     q_weight: torch.Tensor | None, k_weight: torch.Tensor | None, eps: float, world: int,
-                     out: torch.Tensor | None = None, head_major: bool = False) -> torch.Tensor:
-    """q, k, v: [S_l, H*128] (views of the fused QKV output are fine; rows may be strided).
-    rope: fp32 [S_l, 64, 2, 2] or None. Returns the seq->head send buffer
-    [world, 3, H/world, S_l, 128] with q and k RMS-normalised (+ rotated); head_major=True lays
-    it out [H/world, world, 3, S_l, 128] instead, so each local head's blocks for all peers are
-    one contiguous all-to-all buffer (head-by-head pipelining)."""
+def _pack_args(q, k, v, rope, q_weight, k_weight):
+    """Checks shared by the pack entry points; returns (q2, k2, v2, tokens, heads, rope_ptr,
+    rope_row_stride, [q_weight_ptr, k_weight_ptr])."""
     for n, t in (("q", q), ("k", k), ("v", v)):
         _cuda(t, n)
         if t.dim() == 3:
@@ -198,10 +241,6 @@ def qknorm_rope_pack(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, rope: to
         raise H3Error("q, k, v must share shape [tokens, heads*128]")
     if not (q2.stride(0) == k2.stride(0) == v2.stride(0)):
         raise H3Error("q, k, v must share a row stride")
-    H = hd // D
-    if H % world:
-        raise H3Error(f"heads {H} not divisible by world {world}")
-    hl = H // world
     rope_ptr, rope_stride = None, 0
     if rope is not None:
         _cuda(rope, "rope", torch.float32)
@@ -221,6 +260,21 @@ def qknorm_rope_pack(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, rope: to
         if tuple(w.shape) != (D,) or not w.is_contiguous():
             raise H3Error(f"{n} must be contiguous [128] bf16")
         wptr.append(w.data_ptr())
+    return q2, k2, v2, sl, hd // D, rope_ptr, rope_stride, wptr
+
+
+def qknorm_rope_pack(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, rope: torch.Tensor | None,
+                     q_weight: torch.Tensor | None, k_weight: torch.Tensor | None, eps: float, world: int,
+                     out: torch.Tensor | None = None, head_major: bool = False) -> torch.Tensor:
+    """q, k, v: [S_l, H*128] (views of the fused QKV output are fine; rows may be strided).
+    rope: fp32 [S_l, 64, 2, 2] or None. Returns the seq->head send buffer
+    [world, 3, H/world, S_l, 128] with q and k RMS-normalised (+ rotated); head_major=True lays
+    it out [H/world, world, 3, S_l, 128] instead, so each local head's blocks for all peers are
+    one contiguous all-to-all buffer (head-by-head pipelining)."""
+    q2, k2, v2, sl, H, rope_ptr, rope_stride, wptr = _pack_args(q, k, v, rope, q_weight, k_weight)
+    if H % world:
+        raise H3Error(f"heads {H} not divisible by world {world}")
+    hl = H // world
     shape = (hl, world, 3, sl, D) if head_major else (world, 3, hl, sl, D)
     if out is None:
         out = torch.empty(shape, dtype=torch.bfloat16, device=q.device)

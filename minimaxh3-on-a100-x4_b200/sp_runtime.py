@@ -11,6 +11,7 @@ Same module API and behaviour, B200 data path underneath:
   RANK, WORLD                  module constants from the environment   (ref :16-17)
   env SP_TIMING=1, SP_OVERLAP=1, SP_PIECES=N                           (ref :32, :133, :265)
   env SP_OVERLAP=heads         head-by-head all-to-all / attention pipelining (this build)
+  env SP_OVERLAP=peer          all-to-alls fused into pack / attention over peer memory (this build)
 
 What differs, by design:
   * The attention layer runs on libh3attn.so (sm_100a): one fused kernel does the q/k
@@ -353,6 +354,88 @@ def _sp_attn_forward_heads(self, x, rope_freqs=None, transformer_options={}):
         return O.linear(o_hsd, w_out) if w_out is not None else self.out_proj(O.head_to_seq_unpack(o_hsd))
 
 
+_peer_cache = {}
+
+
+def _peer_buffers(s, H, D, dev, slots=1):
+    """Symmetric-memory buffers for the fused exchanges of one layer shape, allocated and
+    rendezvoused once (a collective: every rank reaches it with the same shape): per slot the
+    attention input [3][H/W][W*s][D] that every rank's pack writes into, and the out_proj input
+    [s][H*D] that every rank's attention writes into; device tables of every rank's addresses."""
+    key = (s, H, D, str(dev), slots)
+    if key in _peer_cache:
+        return _peer_cache[key]
+    # plain peer mappings only: the kernels store into peers' buffers, nothing uses multicast
+    os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
+    import torch.distributed._symmetric_memory as symm
+    W, hl = WORLD, H // WORLD
+    group = dist.group.WORLD
+    if hasattr(symm, "enable_symm_mem_for_group"):
+        symm.enable_symm_mem_for_group(group.group_name)
+
+    def table(t, extra_bytes):
+        h = symm.rendezvous(t, group)
+        ptrs = [int(p) + int(h.offset) for p in h.buffer_ptrs]
+        if ptrs[RANK] != t.data_ptr():
+            raise RuntimeError("symmetric buffer addresses do not match the local tensor")
+        return h, torch.tensor([p + extra_bytes for p in ptrs], dtype=torch.int64, device=dev)
+
+    out = []
+    for _ in range(slots):
+        qkv = symm.empty((3, hl, W * s, D), dtype=torch.bfloat16, device=dev)
+        o = symm.empty((s, H * D), dtype=torch.bfloat16, device=dev)
+        hq, qkv_ptrs = table(qkv, 0)
+        ho, o_ptrs = table(o, RANK * hl * D * 2)  # this rank's column block of every peer's [s][H*D]
+        out.append({"qkv": qkv, "o": o, "qkv_ptrs": qkv_ptrs, "o_ptrs": o_ptrs, "handles": (hq, ho)})
+    flag = torch.zeros(1, dtype=torch.float32, device=dev)
+    for b in out:
+        b["flag"] = flag
+    _peer_cache[key] = out
+    return out
+
+
+def _peer_barrier(flag):
+    """Stream-ordered barrier: an NCCL all-reduce of one element completes on a rank only after
+    every rank has enqueued it, i.e. after every rank's preceding kernels (whose peer stores end
+    with a system-scope fence)."""
+    dist.all_reduce(flag)
+
+
+def _sp_attn_forward_peer(self, x, rope_freqs=None, transformer_options={}):
+    """Same math with both all-to-alls fused into the kernels over NVLink peer memory (this build's
+    SP_OVERLAP=peer): the pack writes every head straight into its destination rank's attention
+    input, the attention epilogue writes every query row straight into its destination rank's
+    out_proj input; two stream-ordered barriers per layer. Bit-identical to the blocking path."""
+    if not _SP_ACTIVE:
+        return _orig_attn_forward(self, x, rope_freqs=rope_freqs, transformer_options=transformer_options)
+    if WORLD == 1:
+        return _sp_attn_forward(self, x, rope_freqs=rope_freqs, transformer_options=transformer_options)
+    O = ops()
+    s = x.shape[0]
+    H, D, W = self.heads, self.head_dim, WORLD
+    hl = H // W
+    buf = _peer_buffers(s, H, D, x.device)[0]
+    S_pad = W * s
+    s_kv = _SP_REAL_S if (_SP_REAL_S is not None and _SP_REAL_S < S_pad) else S_pad
+    with _tr("qkv"):
+        w_qkv = _gemm_weight(self.qkv_proj, x)
+        qkv = O.linear(x, w_qkv) if w_qkv is not None else self.qkv_proj(x)
+        q, k, v = qkv.split(H * D, dim=-1)
+        rope, qw, kw = _norm_inputs(self, x, rope_freqs)
+        O.qknorm_rope_pack_peer(q, k, v, rope, qw, kw, self.q_norm.eps, W, buf["qkv_ptrs"], hl * S_pad * D,
+                                S_pad * D, RANK * s)
+    with _tr("a2a_fwd"):
+        _peer_barrier(buf["flag"])  # every rank's q/k/v rows have landed
+    with _tr("fa2_local"):
+        qkvh = buf["qkv"]
+        O.attention_peer(qkvh[0], qkvh[1], qkvh[2], buf["o"], buf["o_ptrs"], s, D, H * D, s_kv=s_kv)
+    with _tr("a2a_inv"):
+        _peer_barrier(buf["flag"])  # every rank's output rows for this rank have landed
+    with _tr("out_proj"):
+        w_out = _gemm_weight(self.out_proj, x)
+        return O.linear(buf["o"], w_out) if w_out is not None else self.out_proj(buf["o"].clone())
+
+
 def _shard_segments(segs, lo, hi):
     out = []
     for a, b, row in segs:
@@ -475,13 +558,14 @@ def install(module=None):
         _orig_mlp_forward = module.MLP.forward
     mode = os.environ.get("SP_OVERLAP", "0")
     overlap = mode == "1"
-    module.Attention.forward = {"1": _sp_attn_forward_overlap, "heads": _sp_attn_forward_heads}.get(
-        mode, _sp_attn_forward)
+    module.Attention.forward = {"1": _sp_attn_forward_overlap, "heads": _sp_attn_forward_heads,
+                                "peer": _sp_attn_forward_peer}.get(mode, _sp_attn_forward)
     module.MiniMaxH3Model.run_blocks = _sp_run_blocks
     if _orig_mlp_forward is not None:
         module.MLP.forward = _sp_mlp_forward
     if RANK == 0:
-        mode = f"overlap(P={_PIECES})" if overlap else ("overlap(heads)" if mode == "heads" else "blocking")
+        mode = f"overlap(P={_PIECES})" if overlap else {"heads": "overlap(heads)", "peer": "fused exchanges (peer)"}.get(
+            mode, "blocking")
         print(f"[sp_runtime] installed (WORLD={WORLD}) - run_blocks + Ulysses attention patched [{mode}]"
               + (" [SP_TIMING]" if _TIMING else ""), flush=True)
 

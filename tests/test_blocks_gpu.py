@@ -77,8 +77,9 @@ def _run(world, S, out_dir, overlap=None):
     return torch.load(os.path.join(out_dir, f"w{world}.pt"))
 
 
-@pytest.mark.parametrize("world,S,overlap", [(2, 1001, None), (2, 1024, "1"), (2, 1001, "heads"), (4, 1003, "heads"),
-                                             (4, 1003, None), (8, 1000, None), (8, 1000, "heads")])
+@pytest.mark.parametrize("world,S,overlap", [(2, 1001, None), (2, 1024, "1"), (2, 1001, "heads"), (2, 1001, "peer"),
+                                             (4, 1003, "heads"), (4, 1003, None), (8, 1000, None), (8, 1000, "heads"),
+                                             (8, 1000, "peer")])
 def test_run_blocks_bit_exact_across_world(world, S, overlap, tmp_path):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")

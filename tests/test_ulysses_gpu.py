@@ -24,7 +24,7 @@ def _port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, S, result_dir):
+def _worker(rank, world, port, S, result_dir, peer=False):
     for p in (PKG, ROOT):
         sys.path.insert(0, p)
     os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port),
@@ -53,14 +53,25 @@ def _worker(rank, world, port, S, result_dir):
         loc = qkv_pad[rank * sl:(rank + 1) * sl].contiguous()
         rope_loc = rope_pad[0, rank * sl:(rank + 1) * sl].contiguous()
         q, k, v = loc.split(H * D, -1)
-        send = h3attn.qknorm_rope_pack(q, k, v, rope_loc, None, None, 1e-6, world)
-        recv = torch.empty_like(send)
-        dist.all_to_all_single(recv, send)
-        qkvh = h3attn.seq_to_head_unpack(recv)
-        o_send = h3attn.attention(qkvh[0], qkvh[1], qkvh[2], s_kv=S, layout="send", world=world)
-        o_recv = torch.empty_like(o_send)
-        dist.all_to_all_single(o_recv, o_send)
-        out = h3attn.head_to_seq_unpack(o_recv.view(H, sl, D))
+        if peer:  # both exchanges fused into the kernels over NVLink peer memory
+            hl = H // world
+            buf = sp_runtime._peer_buffers(sl, H, D, dev)[0]
+            h3attn.qknorm_rope_pack_peer(q, k, v, rope_loc, None, None, 1e-6, world, buf["qkv_ptrs"],
+                                         hl * S_pad * D, S_pad * D, rank * sl)
+            dist.all_reduce(buf["flag"])
+            qkvh = buf["qkv"]
+            h3attn.attention_peer(qkvh[0], qkvh[1], qkvh[2], buf["o"], buf["o_ptrs"], sl, D, H * D, s_kv=S)
+            dist.all_reduce(buf["flag"])
+            out = buf["o"]
+        else:
+            send = h3attn.qknorm_rope_pack(q, k, v, rope_loc, None, None, 1e-6, world)
+            recv = torch.empty_like(send)
+            dist.all_to_all_single(recv, send)
+            qkvh = h3attn.seq_to_head_unpack(recv)
+            o_send = h3attn.attention(qkvh[0], qkvh[1], qkvh[2], s_kv=S, layout="send", world=world)
+            o_recv = torch.empty_like(o_send)
+            dist.all_to_all_single(o_recv, o_send)
+            out = h3attn.head_to_seq_unpack(o_recv.view(H, sl, D))
         h3attn.check_status()
         lo, hi = rank * sl, min((rank + 1) * sl, S)
         ok = torch.equal(out[:hi - lo], ref[lo:hi]) if hi > lo else True
@@ -77,11 +88,14 @@ def _worker(rank, world, port, S, result_dir):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,S", [(2, 4096), (2, 3001), (4, 4096), (8, 4099)])
-def test_ulysses_layer_bit_exact_vs_single_gpu(world, S, tmp_path):
+@pytest.mark.parametrize("world,S,peer", [(2, 4096, False), (2, 3001, False), (4, 4096, False), (8, 4099, False),
+                                          (2, 3001, True), (4, 4096, True), (8, 4099, True)])
+def test_ulysses_layer_bit_exact_vs_single_gpu(world, S, peer, tmp_path):
+    """peer: the exchanges fused into the pack and attention kernels (stores into the destination
+    ranks' symmetric buffers) instead of NCCL all-to-alls plus unpack kernels."""
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
-    mp.start_processes(_worker, args=(world, _port(), S, str(tmp_path)), nprocs=world, start_method="spawn")
+    mp.start_processes(_worker, args=(world, _port(), S, str(tmp_path), peer), nprocs=world, start_method="spawn")
     for r in range(world):
         assert (tmp_path / f"r{r}").read_text() == "ok", r
