@@ -516,16 +516,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xffffffffu,
                       mbar_wait(bar(kBarODone + t), uint32_t(n_kv - 1) & 1u, ctx, kStatusTimeoutO));
     }
+    // Peer outputs (o_peer) are staged in this tile's Q buffer (its last Q*K^T has retired) and
+    // stored as whole 256-byte rows, 16 threads per row, so every warp store writes two contiguous
+    // rows across NVLink instead of 32 scattered 16-byte pieces. Chunk c of row r sits at
+    // c ^ (r & 15) in the staged row.
+    const bool peer = p.o_peer != nullptr;
+    const int r_in = quad * 32 + lane;
+    const uint32_t stage = sbase + kOffQ + uint32_t(t) * kTileBytes;
     if (ok) {
       tc_fence_after();
       const float inv = 1.0f / l_run;
-      const int row = m0 + t * kBlockM + quad * 32 + lane;
+      const int row = m0 + t * kBlockM + r_in;
       const bool valid = row < p.s_q;
       const long long rr = valid ? row : 0;
-      __nv_bfloat16* obase = p.o_peer != nullptr
-                                 ? reinterpret_cast<__nv_bfloat16*>(p.o_peer[rr / p.o_rank_rows])
-                                 : p.o + (rr / p.o_rank_rows) * p.o_rank_stride;
-      __nv_bfloat16* dst = obase + (long long)head * p.o_head_stride + (rr % p.o_rank_rows) * p.o_row_stride;
+      __nv_bfloat16* dst = p.o + (rr / p.o_rank_rows) * p.o_rank_stride + (long long)head * p.o_head_stride +
+                           (rr % p.o_rank_rows) * p.o_row_stride;
 #pragma unroll
       for (int c4 = 0; c4 < 4; ++c4) {
         uint32_t o[32];
@@ -534,13 +539,37 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 16; ++i)
           w[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
-        if (valid) {
+        if (peer) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            st_shared_u4(stage + uint32_t(r_in) * 256u + ((uint32_t(4 * c4 + i) ^ uint32_t(r_in & 15)) << 4),
+                         make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]));
+        } else if (valid) {
           uint4* d4 = reinterpret_cast<uint4*>(dst + c4 * 32);
 #pragma unroll
           for (int i = 0; i < 4; ++i) d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
         }
       }
-      if (p.o_peer != nullptr) __threadfence_system();  // peer stores visible before the host-side barrier
+    }
+    if (peer) {
+      // every warp of the tile reaches this barrier (each wait above is bounded); after an abort the
+      // status word marks the call failed and the rows are not to be used
+      named_bar_sync(1 + t, 128);
+      if (ok) {
+#pragma unroll 4
+        for (int i = 0; i < 16; ++i) {
+          const int kk = i * 128 + r_in;  // chunk kk & 15 of staged row kk >> 4
+          const int sr = kk >> 4, ch = kk & 15;
+          const long long grow = (long long)m0 + t * kBlockM + sr;
+          if (grow < p.s_q) {
+            const uint4 v = ld_shared_u4(stage + uint32_t(sr) * 256u + ((uint32_t(ch) ^ uint32_t(sr & 15)) << 4));
+            __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(p.o_peer[grow / p.o_rank_rows]) +
+                               (long long)head * p.o_head_stride + (grow % p.o_rank_rows) * p.o_row_stride + 8 * ch;
+            *reinterpret_cast<uint4*>(d) = v;
+          }
+        }
+      }
+      __threadfence_system();  // peer stores visible before the host-side barrier
     }
   }
 
