@@ -108,6 +108,35 @@ def test_gemm_rejects_bad_arguments_before_launch(L):
     assert L.h3_gemm_bf16(*bad) == -4                    # output rows shorter than n_out
 
 
+def test_peer_entry_points_reject_bad_arguments_before_launch(L):
+    p, st = ctypes.c_void_p(0x1000), ctypes.c_void_p(0x2000)
+    # pack: q, k, v [10][4*128], 2 ranks, table of 2 addresses
+    ok = [p, p, p, 4 * 128, None, 0, None, None, ctypes.c_float(1e-6), p, 20 * 128, 10 * 128, 0, 10, 4, 2, None]
+    bad = list(ok)
+    bad[9] = None
+    assert L.h3_qknorm_rope_pack_peer(*bad) == -1                 # no address table
+    bad = list(ok)
+    bad[9] = ctypes.c_void_p(0x1004)
+    assert L.h3_qknorm_rope_pack_peer(*bad) == -2                 # table not 8-byte aligned
+    bad = list(ok)
+    bad[15] = 3
+    assert L.h3_qknorm_rope_pack_peer(*bad) == -3                 # heads not divisible into ranks
+    bad = list(ok)
+    bad[10] = 20 * 128 + 4
+    assert L.h3_qknorm_rope_pack_peer(*bad) == -4                 # tensor stride not a multiple of 8
+    # attention: [2][128][128] q/k/v, two destination ranks of 64 rows
+    a = [p, p, p, p, p, 2, 128, 128, 128 * 128, 128, 128 * 128, 128, 64, 128, 256, ctypes.c_float(0.088), st, None]
+    bad = list(a)
+    bad[4] = None
+    assert L.h3_attn_fwd_peer(*bad) == -1                         # no address table
+    bad = list(a)
+    bad[4] = ctypes.c_void_p(0x1004)
+    assert L.h3_attn_fwd_peer(*bad) == -2
+    bad = list(a)
+    bad[6] = 0
+    assert L.h3_attn_fwd_peer(*bad) == -3                         # no query rows
+
+
 def test_no_cpu_path():
     """The binding refuses host tensors instead of computing on the CPU."""
     import torch
