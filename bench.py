@@ -7,26 +7,36 @@ One step = one exact 56x128-head attention layer over S = 42,000 tokens (config 
 the Ulysses layer of config 2 at N>1): each rank starts from its token shard of the fused
 QKV projection output, runs the fused qk-RMSNorm + RoPE + send pack, the seq->head
 all-to-all (N>1), attention over its 56/N heads and the full sequence, and the head->seq
-all-to-all back to token-major rows (N>1). FLOPs per step = 4*S^2*128*56 (5.058e13).
+all-to-all back to token-major rows (N>1). FLOPs per step = 4*S^2*128*56 (5.058e13). An S
+that does not divide by N takes the runtime's pad path (pad rows at the tail, keys stop at S).
 
-Printed by rank 0 as ONE JSON line: value = whole-job TFLOP/s from CUDA events (max over
-ranks), e2e = the same through the public API with the step's input copied from pinned
-host memory and its output read back inside the timed region, roofline of the attention
-kernel against MEASURED_PEAKS.json, the CPU baseline (the reference's own SDPA call on
-this host's cores, bounded sample), and SM clocks sampled during the timed region.
+Printed by rank 0 as ONE JSON line:
+  value          whole-job TFLOP/s from CUDA events (max over ranks)
+  e2e            the same through the public API with the step's input copied from pinned host
+                 memory and its output read back inside the timed region, with the per-rank copy
+                 rates and a plain pinned-copy ceiling measured at the same concurrency
+  roofline       the attention kernel against MEASURED_PEAKS.json
+  cpu_baseline   the reference's own SDPA call at config 0 on this host's cores
+  clocks         SM clocks sampled during the timed region
+  bit_exact_vs_w1 (N>1) every rank's output rows equal, bit for bit, the 1-GPU layer on the
+                 gathered input; the run exits non-zero otherwise
+  vendor_attention (N=1) the reference's GPU call (torch SDPA) at config 1 on the same box
+  run_blocks     config 3: the 50-block MiniMax-H3 forward through the installed runtime (ms per
+                 forward, max over ranks, its own clock record, per-category split; at N>1 also
+                 bit-exact against the 1-GPU forward)
 
 --impl reference times the reference's CPU path for this op (torch SDPA FLASH on the host
-cores, harness/sp_runtime.py:119-121) on bounded samples of the same workload.
+cores, harness/sp_runtime.py:119-121) at config 0 (H=56, S=4096, fp32, seed 0).
 """
 from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -40,7 +50,7 @@ import torch.distributed as dist  # noqa: E402
 METRIC = "ms/layer & TFLOP/s, 56x128 attn S=42k bf16, 1/2/4/8 B200; % dense bf16 peak"
 UNIT = "TFLOP/s"
 HEADS, D = 56, 128
-NVLINK_GBS = 770.0  # measured peer copy per direction per GPU on this pool's B200s (nominal 900)
+NVLINK_GBS = 770.0  # measured peer copy per direction per B200 (nominal 900)
 
 
 def flops_layer(s: int, heads: int = HEADS) -> float:
@@ -76,10 +86,9 @@ def profiled_traffic(name: str, seq: int, heads: int):
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons, sampled every 200 ms from before the warm-up
-    until after the timed region; summary() keeps the samples stamped inside the timed
-    window (mark_start / mark_end), falling back to the whole run when the window was too
-    short to catch one."""
+    """nvidia-smi clocks and throttle reasons, sampled every 200 ms from start() to stop();
+    summary(window) keeps the samples stamped inside a named window (mark(name, "start"/"end")),
+    falling back to the whole run when the window was too short to catch one."""
 
     Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -89,12 +98,12 @@ class ClockSampler:
     def __init__(self, n_gpus: int):
         self.n = n_gpus
         self.proc = None
-        self.t_start = self.t_end = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_bench_{os.getpid()}.csv")
+        self.windows = {}
+        self.tmp = tempfile.TemporaryDirectory(prefix="h3_clocks_")
+        self.path = os.path.join(self.tmp.name, "clocks.csv")
 
     def start(self):
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
                                           "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
@@ -102,21 +111,19 @@ class ClockSampler:
             self.proc = None
         return self
 
-    def mark_start(self):
-        self.t_start = time.time()
-
-    def mark_end(self):
-        self.t_end = time.time()
+    def mark(self, window: str, edge: str):
+        self.windows.setdefault(window, {})[edge] = time.time()
 
     def stop(self):
         if self.proc is not None:
-            time.sleep(0.25)  # one more sample after the window
+            time.sleep(0.25)  # one more sample after the last window
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
             self.f.close()
+            self.proc_done = True
 
     def _rows(self):
         with open(self.path) as f:
@@ -131,11 +138,13 @@ class ClockSampler:
                 except ValueError:
                     continue
 
-    def summary(self):
+    def summary(self, window: str):
         if self.proc is None or not os.path.exists(self.path):
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         rows = list(self._rows())
-        win = [r for r in rows if self.t_start is not None and self.t_start - 0.2 <= r[0] <= self.t_end + 0.2]
+        w = self.windows.get(window, {})
+        t0, t1 = w.get("start"), w.get("end")
+        win = [r for r in rows if t0 is not None and t1 is not None and t0 - 0.2 <= r[0] <= t1 + 0.2]
         scope = "timed region"
         if not win:
             win, scope = rows, "whole run (timed region shorter than the sampling period)"
@@ -146,43 +155,45 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(win), "scope": scope}
 
 
-def cpu_sdpa_sample(s_kv: int, heads: int, rows: int, reps: int, threads: int):
-    """The reference's attention call (SDPA FLASH, sp_runtime.py:119-121) in fp32 on the host
-    cores for `heads` heads x `rows` query rows against all s_kv keys. Returns the per-rep times."""
-    from oracle import sdpa_ref
+# ----------------------------------------------------------------------------- the CPU baseline
+def cpu_config0(reps: int, threads: int):
+    """The reference's attention call (SDPA FLASH, sp_runtime.py:119-121) at config 0 (H=56,
+    S=4096, D=128, fp32, seed 0, RMSNorm + RoPE on q and k) on the host cores. One warm-up run,
+    then `reps` timed runs; returns (per-run seconds, FLOPs per run, sample description)."""
+    from oracle import north_star, sdpa_ref
     torch.set_num_threads(threads)
-    g = torch.Generator().manual_seed(0)
-    q = torch.randn(1, heads, rows, D, generator=g)
-    k = torch.randn(1, heads, s_kv, D, generator=g)
-    v = torch.randn(1, heads, s_kv, D, generator=g)
-    sdpa_ref.attention(q[:, :, :64], k[:, :, :256], v[:, :, :256])  # warm-up
+    H, S = 56, 4096
+    q, k, v = north_star.config_inputs(0, H, S, "cpu")
+    q, k, v = q[None], k[None], v[None]
+    sdpa_ref.attention(q, k, v)  # warm-up
     times = []
     for _ in range(reps):
         t0 = time.perf_counter()
         sdpa_ref.attention(q, k, v)
         times.append(time.perf_counter() - t0)
-    return times
+    sample = (f"config 0: B=1 H={H} S={S} D=128 fp32 seed 0 (RMSNorm + RoPE), the reference's SDPA FLASH call "
+              f"on the CPU, {threads} threads, median of {reps} after one warm-up")
+    return times, flops_layer(S, H), sample
 
 
 def run_reference(args, rank: int, world: int) -> None:
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    heads, rows = 1, 4096  # one bounded sample per step: 1 head x 4096 query rows x all keys
-    torch.set_num_threads(threads)
-    times = cpu_sdpa_sample(args.seq, heads, rows, args.warmup + args.steps, threads)[args.warmup:]
+    times, fl, sample = cpu_config0(args.warmup + args.steps, threads)
+    times = times[args.warmup:]
     per = statistics.median(times)
-    fl = 4.0 * rows * args.seq * D * heads
     val = fl / per / 1e12
-    sample = f"{heads} head x {rows} query rows x {args.seq} keys fp32 per step ({fl:.3g} FLOP)"
     line = {
         "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
         "config": config(args),
-        "cpu_baseline": {"value": val, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": sample + "; torch SDPA FLASH on CPU, the reference's attention call"},
+        "cpu_baseline": {"value": val, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample,
+                         "ms": per * 1e3},
         "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "ms_per_layer_at_s": {"s": args.seq, "ms": flops_layer(args.seq) / (val * 1e12) * 1e3,
+                              "how": "config-0 throughput applied to the arm's layer (4*S^2*128*56 FLOP)"},
     }
     print(json.dumps(line), flush=True)
 
@@ -195,6 +206,26 @@ def config(args):
             "l2": f"inputs larger than L2: {args.batch * args.seq * 3 * HEADS * D * 2 / 1e9:.2f} GB of QKV per step"}
 
 
+# ----------------------------------------------------------------------------- helpers
+def gpu_local_cpus(dev: torch.device):
+    """CPUs on the NUMA node of `dev` (from sysfs), or None when unknown."""
+    try:
+        p = torch.cuda.get_device_properties(dev)
+        bus = f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        with open(f"/sys/bus/pci/devices/{bus}/local_cpulist") as f:
+            spec = f.read().strip()
+    except (AttributeError, OSError, RuntimeError):
+        return None
+    cpus = set()
+    for part in spec.split(","):
+        if "-" in part:
+            a, b = part.split("-")
+            cpus.update(range(int(a), int(b) + 1))
+        elif part:
+            cpus.add(int(part))
+    return cpus or None
+
+
 def run_ours(args, rank: int, world: int, local: int) -> None:
     import h3attn
     import h3_model
@@ -202,14 +233,32 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     dev = torch.device("cuda", local)
     S, H, W = args.seq, HEADS, world
     sampler = ClockSampler(W).start() if rank == 0 else None  # started early: nvidia-smi needs ~1 s
-    if S % W or H % W:
-        raise SystemExit(f"seq {S} and heads {H} must divide by {W}")
-    sl, hl = S // W, H // W
-    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    if H % W:
+        raise SystemExit(f"heads {H} must divide by {W}")
+    sl, hl = -(-S // W), H // W
+    S_pad = sl * W
+    real = max(0, min(sl, S - rank * sl))  # this rank's real (non-pad) rows
+    # host buffers on the GPU's own NUMA node: bind before any pinned allocation (first touch)
+    numa = None
+    if not args.no_numa_bind:
+        cpus = gpu_local_cpus(dev)
+        if cpus:
+            try:
+                os.sched_setaffinity(0, cpus)
+                numa = f"{len(cpus)} CPUs local to the GPU"
+            except OSError:
+                numa = None
     B = args.batch  # independent sequences per step (config 4: CFG cond/uncond, separate seeds)
-    qkv = torch.stack([torch.randn((sl, 3 * H * D), generator=torch.Generator(device=dev).manual_seed(1000 + rank + 7919 * b),
-                                   device=dev, dtype=torch.float32).to(torch.bfloat16) for b in range(B)])
+
+    def make_qkv(b):
+        g = torch.Generator(device=dev).manual_seed(1000 + rank + 7919 * b)
+        x = torch.randn((sl, 3 * H * D), generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+        x[real:] = 0  # pad rows (S not a multiple of W)
+        return x
+
+    qkv = torch.stack([make_qkv(b) for b in range(B)])
     rope = h3_model.rope_freqs_1d(sl, pos0=rank * sl, device=dev)[0].contiguous()
+    rope[real:] = 0
     ones = torch.ones(D, dtype=torch.bfloat16, device=dev)
     eps = 1e-6
     ev_att, ev_a2a = [], []
@@ -236,9 +285,9 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
         if W > 1:
-            o_send = h3attn.attention(qkvh[0], qkvh[1], qkvh[2], layout="send", world=W)
+            o_send = h3attn.attention(qkvh[0], qkvh[1], qkvh[2], s_kv=S, layout="send", world=W)
         else:
-            o = h3attn.attention(qkvh[0], qkvh[1], qkvh[2], layout="token", out=out)
+            o = h3attn.attention(qkvh[0], qkvh[1], qkvh[2], s_kv=S, layout="token", out=out)
         if timed:
             e1.record()
             ev_att.append((e0, e1))
@@ -276,7 +325,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
                 if timed:
                     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                     e0.record(cs)
-                o_send = h3attn.attention(qkvh[0], qkvh[1], qkvh[2], layout="send", world=W)
+                o_send = h3attn.attention(qkvh[0], qkvh[1], qkvh[2], s_kv=S, layout="send", world=W)
                 if timed:
                     e1.record(cs)
                     ev_att.append((e0, e1))
@@ -304,13 +353,14 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         buf = peer_bufs[peer_step[0] % 2]
         peer_step[0] += 1
         q, k, v = x.split(H * D, dim=-1)
-        h3attn.qknorm_rope_pack_peer(q, k, v, rope, ones, ones, eps, W, buf["qkv_ptrs"], hl * S * D, S * D, rank * sl)
+        h3attn.qknorm_rope_pack_peer(q, k, v, rope, ones, ones, eps, W, buf["qkv_ptrs"], hl * S_pad * D, S_pad * D,
+                                     rank * sl)
         barrier(buf["flag"], timed)
         qkvh = buf["qkv"]
         if timed:
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
-        h3attn.attention_peer(qkvh[0], qkvh[1], qkvh[2], buf["o"], buf["o_ptrs"], sl, D, H * D)
+        h3attn.attention_peer(qkvh[0], qkvh[1], qkvh[2], buf["o"], buf["o_ptrs"], sl, D, H * D, s_kv=S)
         if timed:
             e1.record()
             ev_att.append((e0, e1))
@@ -363,21 +413,40 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     sync_all()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if sampler:
-        sampler.mark_start()
+        sampler.mark("layer", "start")
     t0.record()
     for _ in range(args.steps):
         step(qkv, timed=True)
     t1.record()
     sync_all()
     if sampler:
-        sampler.mark_end()
-        sampler.stop()
+        sampler.mark("layer", "end")
     ms = max_over_ranks(t0.elapsed_time(t1) / args.steps)
     att_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in ev_att))
     if W > 1:  # the blocking layer: both exchanges are exposed (nothing runs beside them)
         a2a_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b, _ in ev_a2a) / args.steps)
         a2a_bytes = sum(n for _, _, n in ev_a2a) / args.steps
     h3attn.check_status()
+
+    # ---- W-way output against the 1-GPU layer on the gathered input, bit for bit
+    bit_exact = None
+    if W > 1:
+        mine = torch.stack([o.clone() for o in step(qkv)])  # [B, sl, H*D]
+        ok = True
+        for b in range(B):
+            full = torch.empty((S_pad, 3 * H * D), dtype=torch.bfloat16, device=dev)
+            dist.all_gather_into_tensor(full, qkv[b].contiguous())
+            rope_full = h3_model.rope_freqs_1d(S_pad, device=dev)[0].contiguous()
+            rope_full[S:] = 0
+            q, k, v = full.split(H * D, dim=-1)
+            send1 = h3attn.qknorm_rope_pack(q, k, v, rope_full, ones, ones, eps, 1)
+            ref = h3attn.attention(send1[0, 0], send1[0, 1], send1[0, 2], s_kv=S, layout="token")
+            ok = ok and torch.equal(ref[rank * sl:rank * sl + real], mine[b, :real])
+            del full, send1, ref
+        flag = torch.tensor([0 if ok else 1], device=dev, dtype=torch.int32)
+        dist.all_reduce(flag)
+        bit_exact = int(flag.item()) == 0
+        h3attn.check_status()
 
     # ---- end-to-end through the public API: every step copies its input from pinned host
     # memory and reads its output back. Copies run on their own streams with two device
@@ -431,6 +500,36 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     if not torch.equal(host_out[(e2e_warm + e2e_n - 1) % 2], torch.stack([r.cpu() for r in step(qkv)])):
         raise SystemExit("end-to-end output differs from the device-resident run")
 
+    # the copies alone, every rank at once: the ceiling the e2e pipeline runs against
+    def copy_ms(dst, src, reps=3):
+        sync_all()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            dst.copy_(src, non_blocking=True)
+        b.record()
+        torch.cuda.synchronize()
+        return max_over_ranks(a.elapsed_time(b) / reps)
+
+    h2d_bytes, d2h_bytes = qkv.numel() * 2, B * sl * H * D * 2  # per rank per step
+    h2d_alone = copy_ms(dev_in[0], host_in)
+    d2h_alone = copy_ms(host_out[0], dev_out[0])
+    del dev_in, dev_out, host_in, host_out
+
+    # ---- the reference's own GPU call at config 1 on the same box (context for the kernel's speed)
+    vendor = None
+    if W == 1 and B == 1 and not args.no_vendor:
+        vendor = vendor_attention(qkv[0], rope, ones, eps, S, att_ms)
+    del qkv
+    torch.cuda.empty_cache()
+
+    # ---- config 3: the 50-block run_blocks forward through the installed runtime
+    rb = None
+    if args.rb_blocks > 0 and B == 1:
+        rb = run_blocks_bench(args, rank, W, dev, sampler, max_over_ranks, sync_all)
+
+    if sampler:
+        sampler.stop()
     if rank != 0:
         return
     fl = flops_layer(S) * B
@@ -442,6 +541,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     # the unpack and attention once per local head when pipelined by heads
     per_step = 2 if W == 1 or peer_bufs is not None else (4 if heads_per_launch == hl else 2 + 2 * hl)
     launches = per_step * B * args.steps
+    e2e_bound_ms = max(ms, h2d_alone, d2h_alone)
     line = {
         "metric": METRIC, "value": fl / (ms * 1e-3) / 1e12, "unit": UNIT, "n_gpus": W, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
@@ -452,9 +552,17 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
                      "kernel_ms": att_ms, "flop_per_launch": att_fl},
         "e2e": {"value": fl / (e2e_ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": e2e_ms,
                 "method": "steady-state pipeline: step i+1's upload and step i-1's readback overlap step i",
-                "h2d_bytes_per_step": qkv.numel() * 2 * W, "d2h_bytes_per_step": B * sl * H * D * 2 * W},
+                "h2d_bytes_per_step": h2d_bytes * W, "d2h_bytes_per_step": d2h_bytes * W,
+                "h2d_gbs_per_rank": h2d_bytes / (e2e_ms * 1e-3) / 1e9,
+                "d2h_gbs_per_rank": d2h_bytes / (e2e_ms * 1e-3) / 1e9,
+                "copy_ceiling": {"h2d_ms": h2d_alone, "d2h_ms": d2h_alone,
+                                 "h2d_gbs_per_rank": h2d_bytes / (h2d_alone * 1e-3) / 1e9,
+                                 "d2h_gbs_per_rank": d2h_bytes / (d2h_alone * 1e-3) / 1e9,
+                                 "how": f"each copy alone, all {W} ranks at once, pinned host memory"
+                                        + (f" on {numa}" if numa else "")},
+                "bound_ms": e2e_bound_ms, "frac_of_bound": e2e_bound_ms / e2e_ms},
         "gpu_launches": launches,
-        "clocks": sampler.summary() if sampler else None,
+        "clocks": sampler.summary("layer") if sampler else None,
     }
     if W > 1 and peer_bufs is not None:
         # the exchanges are stores of the pack and attention kernels; only the barriers stand alone
@@ -467,18 +575,127 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         key = "exposed_ms_per_step" if args.overlap == "none" else "comm_stream_ms_per_step_overlapped"
         line["a2a"] = {key: a2a_ms, "bytes_sent_per_gpu_per_step": a2a_bytes,
                        "achieved_gbs_per_gpu": gbs, "frac_of_nvlink": gbs / NVLINK_GBS,
-                       "nvlink_ref": f"{NVLINK_GBS:.0f} GB/s per direction per GPU (measured peer copy on this pool)",
+                       "nvlink_ref": f"{NVLINK_GBS:.0f} GB/s per direction per GPU (measured peer copy)",
                        "frac_of_step": a2a_ms / ms}
     if W == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        heads, rows = 4, 4096
-        times = cpu_sdpa_sample(S, heads, rows, 5, threads)
+        times, cfl, sample = cpu_config0(3, threads)
         per = statistics.median(times)
-        cfl = 4.0 * rows * S * D * heads
         line["cpu_baseline"] = {"value": cfl / per / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
-                                "sample": f"{heads} heads x {rows} query rows x {S} keys fp32 ({cfl:.3g} FLOP), "
-                                          f"median of 5; torch SDPA FLASH on CPU (the reference's attention call)"}
+                                "sample": sample, "ms": per * 1e3}
+    if vendor is not None:
+        line["vendor_attention"] = vendor
+    if rb is not None:
+        line["run_blocks"] = rb
+    if bit_exact is not None:
+        line["bit_exact_vs_w1"] = bit_exact
     print(json.dumps(line), flush=True)
+    if bit_exact is False or (rb is not None and rb.get("bit_exact_vs_w1") is False):
+        raise SystemExit("W-way output differs from the 1-GPU output")
+
+
+def vendor_attention(x, rope, ones, eps, S, our_ms):
+    """torch SDPA (the reference's call, sp_runtime.py:119-121) on the bench's own packed q, k, v
+    [1, 56, S, 128] bf16, by backend: 1 warm-up + 3 timed calls each, CUDA events."""
+    import h3attn
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    q, k, v = x.split(HEADS * D, dim=-1)
+    send = h3attn.qknorm_rope_pack(q, k, v, rope, ones, ones, eps, 1)
+    qh, kh, vh = (send[0, i][None] for i in range(3))
+    out = {}
+    for name, backend in (("flash", SDPBackend.FLASH_ATTENTION), ("cudnn", SDPBackend.CUDNN_ATTENTION)):
+        try:
+            with sdpa_kernel([backend]):
+                torch.nn.functional.scaled_dot_product_attention(qh, kh, vh)
+                torch.cuda.synchronize()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                for _ in range(3):
+                    torch.nn.functional.scaled_dot_product_attention(qh, kh, vh)
+                b.record()
+                torch.cuda.synchronize()
+            ms = a.elapsed_time(b) / 3
+            out[name] = {"ms": ms, "tflops": flops_layer(S) / (ms * 1e-3) / 1e12, "ours_speedup": ms / our_ms}
+        except RuntimeError as exc:
+            out[name] = {"unavailable": str(exc).splitlines()[0][:160]}
+    out["call"] = "torch.nn.functional.scaled_dot_product_attention, [1,56,S,128] bf16, per SDPBackend"
+    return out
+
+
+def run_blocks_bench(args, rank, W, dev, sampler, max_over_ranks, sync_all):
+    """Config 3: the 50-block MiniMax-H3 denoiser forward (run_blocks) through the installed runtime,
+    as the reference's full-step harness measures it (harness/sp_full_step.py:48-93): hidden 5376,
+    56x128 heads, SwiGLU 14336, AdaLN from a sinusoidal t=500 embedding, bf16 weights ~N(0, 0.02),
+    the packed [512 | 1024 | 1464 | 39000] sequence of x ~N(0, 1). Returns the run_blocks record."""
+    import h3_model as M
+    import h3attn
+    import sp_runtime
+
+    sp_runtime.init()
+    S = args.rb_seq
+    blocks = args.rb_blocks
+    model = M.MiniMaxH3Model(n_blocks=blocks, dtype=torch.bfloat16, device=dev)
+    g = torch.Generator(device=dev).manual_seed(3)  # the same weights on every rank
+    with torch.no_grad():
+        for m in model.modules():
+            if isinstance(m, torch.nn.Linear):
+                m.weight.normal_(0.0, 0.02, generator=g)
+    segs = [(a, min(b, S), r) for a, b, r in M.H3_SEGMENTS if a < S]
+    h = torch.randn((S, M.HIDDEN), generator=torch.Generator(device=dev).manual_seed(4), device=dev).to(torch.bfloat16)
+    t_emb = M.timestep_embedding(torch.full((len(segs),), 500.0, device=dev)).to(torch.bfloat16)
+    rope = M.rope_freqs_1d(S, device=dev)
+    sp_runtime.install(M)
+
+    def fwd():
+        with torch.no_grad():
+            return model.run_blocks(h, t_emb, segs, rope, {})
+
+    fwd()  # warm-up (also runs the runtime's status check)
+    sync_all()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if sampler:
+        sampler.mark("run_blocks", "start")
+    a.record()
+    for _ in range(args.rb_steps):
+        out = fwd()
+    b.record()
+    sync_all()
+    if sampler:
+        sampler.mark("run_blocks", "end")
+    ms = max_over_ranks(a.elapsed_time(b) / args.rb_steps)
+    h3attn.check_status()
+    # one more forward with the runtime's per-category CUDA-event timing (SP_TIMING), MAX over ranks
+    sp_runtime._TIMING = True
+    fwd()
+    sp_runtime._TIMING = False
+    cats = sp_runtime.get_timing()
+    cat_ms = {k: max_over_ranks(cats.get(k, 0.0)) for k in sp_runtime.CATEGORIES}
+    rec = {"ms": ms, "forwards": args.rb_steps, "blocks": blocks, "seq_len": S,
+           "tflops": forward_flops(S, blocks) / (ms * 1e-3) / 1e12, "flop_per_forward": forward_flops(S, blocks),
+           "categories_ms": {k: round(v, 1) for k, v in cat_ms.items()},
+           "clocks": sampler.summary("run_blocks") if sampler else None}
+    if W > 1:
+        # the same forward on this GPU alone (the runtime's W=1 seam, same kernels), compared bit for bit
+        world, rnk = sp_runtime.WORLD, sp_runtime.RANK
+        sp_runtime.WORLD, sp_runtime.RANK = 1, 0
+        try:
+            one = fwd()
+        finally:
+            sp_runtime.WORLD, sp_runtime.RANK = world, rnk
+        flag = torch.tensor([0 if torch.equal(one, out) else 1], device=dev, dtype=torch.int32)
+        dist.all_reduce(flag)
+        rec["bit_exact_vs_w1"] = int(flag.item()) == 0
+    sp_runtime.uninstall()
+    del model, h, out
+    torch.cuda.empty_cache()
+    return rec
+
+
+def forward_flops(s: int, blocks: int, hidden=5376, heads=56, head_dim=128, ffn=14336) -> float:
+    """Projection GEMMs (qkv, out, fc1 with both SwiGLU halves, fc2) plus attention, per forward."""
+    hd = heads * head_dim
+    gemm = 2.0 * s * (hidden * 3 * hd + hd * hidden + hidden * 2 * ffn + ffn * hidden)
+    return blocks * (gemm + flops_layer(s, heads))
 
 
 def main():
@@ -489,9 +706,14 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--seq", type=int, default=42000)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-vendor", action="store_true", help="skip timing torch SDPA at N=1")
+    ap.add_argument("--no-numa-bind", action="store_true", help="leave host buffers wherever the OS puts them")
     ap.add_argument("--batch", type=int, default=1, help="independent sequences per step (config 4: 2)")
     ap.add_argument("--overlap", default="none", choices=["none", "heads", "peer"],
                     help="W>1: exchanges pipelined head by head, or fused into the kernels over peer memory")
+    ap.add_argument("--rb-blocks", type=int, default=50, help="config 3 run_blocks forward depth (0: skip)")
+    ap.add_argument("--rb-seq", type=int, default=42000)
+    ap.add_argument("--rb-steps", type=int, default=2, help="timed run_blocks forwards")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))

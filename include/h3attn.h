@@ -13,6 +13,8 @@
  * must be zero before a launch; it is sticky (kernels only ever write non-zero codes).
  *
  * Threading: calls keep no global mutable state; distinct streams may call concurrently.
+ * The one exception is h3_attn_layer_noalloc: every call shares one static device array, so
+ * its calls must not overlap on the GPU (see its comment).
  */
 #ifndef H3ATTN_H_
 #define H3ATTN_H_
@@ -72,30 +74,15 @@ int h3_attn_fwd(const void* q, const void* k, const void* v, void* o, int64_t n_
                 float softmax_scale, int32_t* status, void* stream);
 
 /* h3_attn_fwd with an explicit kernel schedule (a tuning hook; h3_attn_fwd uses the
- * default). All variants compute the same attention within the same tolerance:
- *   0  two softmax warpgroups run freely, exp2 on MUFU
+ * default). All variants compute the same attention within the same tolerance; 1, 10 and 11
+ * are bit-identical to 0 (same arithmetic in another schedule):
+ *   0  two softmax warpgroups run freely, exp2 on MUFU (the default)
  *   1  softmax warpgroups alternate their exp phase (ping-pong token), exp2 on MUFU
  *   2  ping-pong, every 4th element's exp2 on the FMA pipe (degree-3 minimax polynomial)
  *   3  ping-pong, every 8th element on the FMA pipe
  *   4  ping-pong, every 2nd element on the FMA pipe
- *   5  four threads per query row (16-lane TMEM shapes), exp2 on MUFU
- *   6  as 5 with the ping-pong token
- *   7, 8, 9  as 5 with 1/8, 1/4, 1/2 of the keys' exp2 on the FMA pipe
  *   10 as 0 with one MMA-issuing thread per Q tile; 11 as 10 with the ping-pong token;
  *   12 as 10 with every 8th element's exp2 on the FMA pipe
- *   13 SM-pair kernel: two-CTA clusters, cta_group::2 MMAs (each SM reads half of every K/V
- *      tile), one 128-row Q tile per CTA with S double-buffered in TMEM
- *   14 as 13 with two softmax warps per TMEM lane quarter, each owning 64 keys of every row
- *   15 as 13 with two softmax warps per TMEM lane quarter, each owning 16 rows (four
- *      threads per row)
- *   16 as 10 with P in shared memory instead of S's TMEM columns: S is released when the
- *      softmax has loaded it and the next Q*K^T runs under the softmax
- *   17 as 16 with the two tiles' softmax warpgroups taking turns for each 64-key exp phase
- *   18 as 0 with speculative exponentials: each half is exponentiated against the running max
- *      while its own max is taken, and redone in the rare case the max jumps (same results)
- *   19 as 18 with one MMA-issuing thread per Q tile (as 10)
- *   20 as 0 on SM pairs: two-CTA clusters, every MMA a cta_group::2 pair MMA on the same Q tile of
- *      both CTAs, each SM staging half of every K (by keys) and V (by head dimension) tile
  * Returns H3_ERR_UNSUPPORTED for any other value. */
 int h3_attn_fwd_variant(const void* q, const void* k, const void* v, void* o, int64_t n_heads, int64_t s_q,
                         int64_t s_kv, int64_t q_head_stride, int64_t q_row_stride, int64_t kv_head_stride,
@@ -103,7 +90,7 @@ int h3_attn_fwd_variant(const void* q, const void* k, const void* v, void* o, in
                         int64_t o_row_stride, float softmax_scale, int32_t* status, int32_t variant, void* stream);
 
 /* Phase profiler (diagnostics; cf. the clock64 phase counters of the reference kernel,
- * attn_sm80/fa3_sm80_h3.cu:96-105, :572-582): runs variants 0-3, 5, 6, 8, 10, 11, 13-18 or 20 and records clock64()
+ * attn_sm80/fa3_sm80_h3.cu:96-105, :572-582): runs variants 0-3, 10 or 11 and records clock64()
  * stamps of CTA (0, 0) for the first trace_iters KV iterations into the device buffer
  *   trace[((role * trace_iters) + j) * 8 + point]   (int64, 3 * trace_iters * 8 entries)
  * role 0/1 = softmax warpgroup of Q tile 0/1: points 0 before the S wait, 1 S ready,
@@ -153,8 +140,10 @@ int h3_head_to_seq_unpack(const void* recv, void* out, int64_t n_heads, int64_t 
 /* The two all-to-alls of the Ulysses layer fused into the kernels that produce their data, over
  * NVLink peer memory (replacing a2a_seq_to_head + its receive permute, harness/sp_runtime.py:67-71,
  * and a2a_head_to_seq + the head->seq transpose, :73-77 and :125). rank_base / o_peer are DEVICE
- * arrays of W addresses, one per destination rank, each mapped into this process (e.g. symmetric
+ * arrays of n_ranks addresses, one per destination rank, each mapped into this process (e.g. symmetric
  * memory); the caller orders the writes of all ranks before any read with a stream-ordered barrier.
+ * A table too short for the call (n_heads / heads_per_rank > n_ranks for the pack, s_q > n_ranks *
+ * o_rank_rows for the attention) is rejected with H3_ERR_SHAPE before anything is enqueued.
  *
  * h3_qknorm_rope_pack_peer: as h3_qknorm_rope_pack, but head g of token t goes to rank
  *   r = g / heads_per_rank at rank_base[r] + tensor*tensor_stride + (g % heads_per_rank)*head_stride
@@ -167,12 +156,12 @@ int h3_head_to_seq_unpack(const void* recv, void* out, int64_t n_heads, int64_t 
  *   fence so their peer stores are visible to the barrier that follows. */
 int h3_qknorm_rope_pack_peer(const void* q, const void* k, const void* v, int64_t in_row_stride, const float* rope,
                              int64_t rope_row_stride, const void* q_weight, const void* k_weight, float eps,
-                             const uint64_t* rank_base, int64_t tensor_stride, int64_t head_stride,
+                             const uint64_t* rank_base, int64_t n_ranks, int64_t tensor_stride, int64_t head_stride,
                              int64_t row_offset, int64_t s_l, int64_t n_heads, int64_t heads_per_rank, void* stream);
 int h3_attn_fwd_peer(const void* q, const void* k, const void* v, void* o_local, const uint64_t* o_peer,
-                     int64_t n_heads, int64_t s_q, int64_t s_kv, int64_t q_head_stride, int64_t q_row_stride,
-                     int64_t kv_head_stride, int64_t kv_row_stride, int64_t o_rank_rows, int64_t o_head_stride,
-                     int64_t o_row_stride, float softmax_scale, int32_t* status, void* stream);
+                     int64_t n_ranks, int64_t n_heads, int64_t s_q, int64_t s_kv, int64_t q_head_stride,
+                     int64_t q_row_stride, int64_t kv_head_stride, int64_t kv_row_stride, int64_t o_rank_rows,
+                     int64_t o_head_stride, int64_t o_row_stride, float softmax_scale, int32_t* status, void* stream);
 
 /* Row-independent projection GEMM, bf16 in, fp32 accumulate, bf16 out:
  *   epilogue 0: c[m][n] = sum_k a[m][k] * w[n][k]                  (w has n_out rows)
@@ -217,6 +206,12 @@ int h3_gated_residual(const void* x, int64_t x_row_stride, const void* y, int64_
  *                   exactly as the softmax warps write P) */
 int h3_tile_kat_qk(const void* q, const void* k, float* s_out, int32_t* status, void* stream);
 int h3_tile_kat_pv(const void* p, const void* v, float* o_out, int32_t* status, void* stream);
+/* Bounded-wait known-answer test (the failure path of every kernel here, on purpose): one CTA
+ * starts a TMA load of tile[128][128] bf16, then waits up to limit_ns nanoseconds (1 us .. 10 s)
+ * on an mbarrier that nothing ever completes. When the limit passes it writes
+ * H3_STATUS_TIMEOUT_KAT into *status, drains its copy, frees its tensor memory and returns,
+ * leaving the device usable; h3_status_read() then returns H3_STATUS_TIMEOUT_KAT. */
+int h3_wait_kat(const void* tile, int64_t limit_ns, int32_t* status, void* stream);
 /* The same through an SM pair (tcgen05.mma.cta_group::2, M = 256, two-CTA cluster):
  *   h3_tile_kat_pair_qk: s_out[256][128] = q[256][128] . k[128][128]^T (CTA r: q rows 128r.., keys 64r..)
  *   h3_tile_kat_pair_pv: o_out[256][128] = p[256][128] . v[128][128]   (CTA r: p rows 128r.., v cols 64r..) */

@@ -23,12 +23,6 @@
 #include <cstdio>
 
 namespace h3 {
-namespace pair {
-int launch_attn(const void* q, const void* k, const void* v, void* o, long long n_heads, long long s_q, long long s_kv,
-                long long q_head_stride, long long q_row_stride, long long kv_head_stride, long long kv_row_stride,
-                long long o_rank_rows, long long o_rank_stride, long long o_head_stride, long long o_row_stride,
-                float scale_log2, int* status, int variant, long long* prof, int prof_iters, cudaStream_t st);
-}  // namespace pair
 namespace attn {
 
 constexpr int kBlockM = 128;
@@ -172,8 +166,7 @@ __device__ __forceinline__ float ex2_mixed(float x, int idx) {
 // kDual: one MMA-issuing thread per Q tile (warps 1 and 3) instead of one for both, so a
 // tile's P*V never waits behind the other tile's P hand-off; shared K/V stages are released
 // by both (arrival count 2) and each thread's commits track only its own MMAs.
-// kSpec: speculative exponentials (see the softmax loop).
-template <bool kPingPong, int kEmu, bool kProf, bool kDual = false, bool kSpec = false>
+template <bool kPingPong, int kEmu, bool kProf, bool kDual = false>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                     const __grid_constant__ CUtensorMap tmap_v, const Params p) {
@@ -436,20 +429,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int h = 0; h < 2; ++h) {
         float l0, l1, l2, l3;
         uint32_t pk[32];
-        // exponentials of this half against m_run (and, when asked, the half's raw max on the way).
-        // kSpec stores P to TMEM in two 16-column chunks as it goes (16 packed words live instead
-        // of 32); a redo overwrites them before the hand-off.
-        auto exps = [&](bool with_max, float& mx) {
+        // h = 0: S_t(j) ready implies every earlier P*V of this tile has retired; h = 1: O holds
+        // the first half of P_t(j) once o_done_a (phase j) completes
+        auto do_rescale = [&](float m_new) -> bool {
+          return h == 0 ? rescale(m_new, 0, 0, true) : rescale(m_new, bar(kBarODoneA + t), uint32_t(j) & 1u, false);
+        };
+        // every half holds at least one live key except possibly the second half of the last tile
+        float mx0 = s[64 * h], mx1 = s[64 * h + 1], mx2 = s[64 * h + 2], mx3 = s[64 * h + 3];
+#pragma unroll
+        for (int i = 4; i < 64; i += 4) {
+          mx0 = fmaxf(mx0, s[64 * h + i]);
+          mx1 = fmaxf(mx1, s[64 * h + i + 1]);
+          mx2 = fmaxf(mx2, s[64 * h + i + 2]);
+          mx3 = fmaxf(mx3, s[64 * h + i + 3]);
+        }
+        const float m_new = fmaxf(m_run, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * c);
+        if (j == 0 && h == 0) {
+          m_run = m_new;
+        } else if (!(ok = do_rescale(m_new))) {
+          break;
+        }
+        prof_mark<kProf>(p, rec, t, j, 3 + 2 * h);
+        // exponentials of this half against m_run
+        {
           const float neg_m = -m_run;
           l0 = l1 = l2 = l3 = 0.f;
-          float x0 = s[64 * h], x1 = s[64 * h + 1];
 #pragma unroll
           for (int i = 0; i < 32; i += 2) {
             const int e = 64 * h + 2 * i;
-            if (with_max) {
-              x0 = fmaxf(x0, fmaxf(s[e], s[e + 2]));
-              x1 = fmaxf(x1, fmaxf(s[e + 1], s[e + 3]));
-            }
             const float e0 = ex2_mixed<kEmu>(fmaf(s[e], c, neg_m), e);
             const float e1 = ex2_mixed<kEmu>(fmaf(s[e + 1], c, neg_m), e + 1);
             const float e2 = ex2_mixed<kEmu>(fmaf(s[e + 2], c, neg_m), e + 2);
@@ -460,52 +467,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             l3 += e3;
             pk[i] = pack_bf16x2(e0, e1);
             pk[i + 1] = pack_bf16x2(e2, e3);
-            if (kSpec && (i == 14 || i == 30)) {
-              uint32_t* chunk = pk + (i - 14);
-              tmem_st16(tP + 32 * h + (i - 14), *reinterpret_cast<uint32_t(*)[16]>(chunk));
-            }
           }
-          mx = fmaxf(x0, x1);
-        };
-        // h = 0: S_t(j) ready implies every earlier P*V of this tile has retired; h = 1: O holds
-        // the first half of P_t(j) once o_done_a (phase j) completes
-        auto do_rescale = [&](float m_new) -> bool {
-          return h == 0 ? rescale(m_new, 0, 0, true) : rescale(m_new, bar(kBarODoneA + t), uint32_t(j) & 1u, false);
-        };
-        if (!kSpec || (j == 0 && h == 0)) {
-          // every half holds at least one live key except possibly the second half of the last tile
-          float mx0 = s[64 * h], mx1 = s[64 * h + 1], mx2 = s[64 * h + 2], mx3 = s[64 * h + 3];
-#pragma unroll
-          for (int i = 4; i < 64; i += 4) {
-            mx0 = fmaxf(mx0, s[64 * h + i]);
-            mx1 = fmaxf(mx1, s[64 * h + i + 1]);
-            mx2 = fmaxf(mx2, s[64 * h + i + 2]);
-            mx3 = fmaxf(mx3, s[64 * h + i + 3]);
-          }
-          const float m_new = fmaxf(m_run, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * c);
-          if (j == 0 && h == 0) {
-            m_run = m_new;
-          } else if (!(ok = do_rescale(m_new))) {
-            break;
-          }
-          prof_mark<kProf>(p, rec, t, j, 3 + 2 * h);
-          float unused;
-          exps(false, unused);
-        } else {
-          // kSpec: exponentiate against the running max first and take the half's max in the same
-          // pass; the rare half whose max jumps by more than 2^8 rescales and exponentiates again.
-          // Same decisions and values as the max-first order, off the softmax -> P*V chain.
-          float mx;
-          exps(true, mx);
-          const float m_new = fmaxf(m_run, mx * c);
-          const bool again = __any_sync(0xffffffffu, m_new > m_run + kRescaleThreshold);
-          if (!(ok = do_rescale(m_new))) break;
-          if (again) exps(false, mx);
-          prof_mark<kProf>(p, rec, t, j, 3 + 2 * h);
         }
         if (kPingPong && h == 1) mbar_arrive(bar(kBarTok + (t ^ 1)));  // hand the exp phase over
         l_run += (l0 + l1) + (l2 + l3);
-        if (!kSpec) tmem_st32(tP + 32 * h, pk);
+        tmem_st32(tP + 32 * h, pk);
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(bar(h == 0 ? kBarPFullA + t : kBarPFullB + t));
@@ -552,10 +518,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (peer) {
-      // every warp of the tile reaches this barrier (each wait above is bounded); after an abort the
-      // status word marks the call failed and the rows are not to be used
-      named_bar_sync(1 + t, 128);
-      if (ok) {
+      // every warp of the tile reaches this barrier (each wait above is bounded). The copy-out reads
+      // rows that other warps staged, so the tile sends nothing unless all four warps finished:
+      // after an abort no peer receives stale staging rows, and the status word marks the call failed
+      const bool tile_ok = named_bar_and(1 + t, 128, ok);
+      if (tile_ok) {
 #pragma unroll 4
         for (int i = 0; i < 16; ++i) {
           const int kk = i * 128 + r_in;  // chunk kk & 15 of staged row kk >> 4
@@ -570,679 +537,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       __threadfence_system();  // peer stores visible before the host-side barrier
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 2) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
-}
-
-// ------------------------------------------------------------------ kernel v2: four threads per row
-// 16 softmax warps (8 per Q tile) + TMA producer warp + MMA warp = 576 threads. Softmax warp w
-// covers TMEM lanes 32*(w&3) + 16*((w>>2)&1) .. +15 of tile w>>3 through the 16-lane shapes, so
-// each query row is held by a quad of threads (32 of its 128 keys each, as adjacent pairs) and
-// each thread holds two rows: row max/sum are two quad shuffles, and every thread's work per
-// KV tile is a quarter of a row-per-thread layout's, which shortens the softmax -> P*V -> next
-// Q*K^T chain that bounds the kernel. P of keys 0..63 goes to S columns 32..63, P of keys
-// 64..127 to columns 96..127 (each already consumed), so each 64-key half of S is loaded only
-// when it is processed.
-constexpr int kThreadsV2 = 576;
-constexpr int kWarpProducerV2 = 16;
-constexpr int kWarpMmaV2 = 17;
-
-template <bool kPingPong, int kEmu, bool kProf>
-__global__ void __launch_bounds__(kThreadsV2, 1)
-    attn_fwd_v2_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
-                       const __grid_constant__ CUtensorMap tmap_v, const Params p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const uint32_t sbase = smem_u32(smem);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBars);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  auto bar = [&](int i) { return smem_u32(&bars[i]); };
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int head = blockIdx.y;
-  const int m0 = blockIdx.x * kRowsPerCta;
-  const int n_kv = p.n_kv_tiles;
-
-  if (threadIdx.x == 0) {
-    mbar_init(bar(kBarQFull), 1);
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(bar(kBarKVFull + s), 1);
-      mbar_init(bar(kBarKVEmpty + s), 1);
-    }
-    for (int t = 0; t < 2; ++t) {
-      mbar_init(bar(kBarSFull + t), 1);
-      mbar_init(bar(kBarPFullA + t), 256);
-      mbar_init(bar(kBarPFullB + t), 256);
-      mbar_init(bar(kBarODoneA + t), 1);
-      mbar_init(bar(kBarODone + t), 1);
-      mbar_init(bar(kBarTok + t), 256);
-    }
-    mbar_init(bar(kBarDrain), 1);
-    *abort_flag = (*reinterpret_cast<volatile int*>(p.status) != 0) ? 1 : 0;
-    fence_mbar_init();
-  }
-  if (warp == kWarpProducerV2) {
-    if (lane == 0) {
-      tma_prefetch_desc(&tmap_q);
-      tma_prefetch_desc(&tmap_k);
-      tma_prefetch_desc(&tmap_v);
-    }
-    tmem_alloc(smem_u32(tmem_slot), 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  const WaitCtx ctx{abort_flag, p.status};
-  const bool grid_aborted = *abort_flag != 0;
-
-  if (warp == kWarpProducerV2) {
-    // ------------------------------------------------------------ TMA producer
-    if (lane == 0 && !grid_aborted) {
-      const uint32_t sq = sbase + kOffQ;
-      const uint32_t skv = sbase + kOffKV;
-      mbar_expect_tx(bar(kBarQFull), 2 * kTileBytes);
-      for (int t = 0; t < 2; ++t)
-        for (int hh = 0; hh < 2; ++hh)
-          tma_load_3d(sq + t * kTileBytes + hh * kHalfBytes, &tmap_q, bar(kBarQFull), hh * 64, m0 + t * kBlockM,
-                      head);
-      int it = 0;
-      for (int j = 0; j < n_kv; ++j) {
-        bool ok = true;
-        for (int kv = 0; kv < 2; ++kv, ++it) {
-          const int st = it % kStages;
-          const uint32_t ph = uint32_t(it / kStages) & 1u;
-          if (!mbar_wait(bar(kBarKVEmpty + st), ph ^ 1u, ctx, kStatusTimeoutKV)) {
-            ok = false;
-            break;
-          }
-          const CUtensorMap* m = kv ? &tmap_v : &tmap_k;
-          mbar_expect_tx(bar(kBarKVFull + st), kTileBytes);
-          tma_load_3d(skv + st * kTileBytes, m, bar(kBarKVFull + st), 0, j * kBlockN, head);
-          tma_load_3d(skv + st * kTileBytes + kHalfBytes, m, bar(kBarKVFull + st), 64, j * kBlockN, head);
-        }
-        if (!ok) break;
-      }
-      drain_wait(bar(kBarQFull), 0, p.status);
-      for (int st = 0; st < kStages; ++st) {
-        const int cnt = it / kStages + (st < it % kStages ? 1 : 0);
-        if (cnt > 0) drain_wait(bar(kBarKVFull + st), uint32_t(cnt - 1) & 1u, p.status);
-      }
-    }
-  } else if (warp == kWarpMmaV2) {
-    // ------------------------------------------------------------ MMA issuer (as in v1; P halves at S+32, S+96)
-    if (lane == 0 && !grid_aborted) {
-      const uint32_t sq = sbase + kOffQ;
-      const uint32_t skv = sbase + kOffKV;
-      const bool rec = blockIdx.x == 0 && blockIdx.y == 0;
-      auto wait_full = [&](int st_it) -> bool {
-        return mbar_wait(bar(kBarKVFull + st_it % kStages), uint32_t(st_it / kStages) & 1u, ctx, kStatusTimeoutKV);
-      };
-      bool ok = mbar_wait(bar(kBarQFull), 0, ctx, kStatusTimeoutQ) && wait_full(0);
-      if (ok) {
-        tc_fence_after();
-        issue_qk(tmem + col_s(0), sq, skv);
-        mma_commit(bar(kBarSFull + 0));
-        issue_qk(tmem + col_s(1), sq + kTileBytes, skv);
-        mma_commit(bar(kBarSFull + 1));
-        mma_commit(bar(kBarKVEmpty + 0));
-      }
-      for (int j = 0; ok && j < n_kv; ++j) {
-        prof_mark<kProf>(p, rec, 2, j, 0);
-        const int it_v = 2 * j + 1, it_k = 2 * j + 2;
-        const bool next = j + 1 < n_kv;
-        if (!(ok = wait_full(it_v))) break;  // TMA-fed smem: no tcgen05 fence needed
-        const uint32_t sv = skv + (it_v % kStages) * kTileBytes;
-        const uint32_t sk = skv + (it_k % kStages) * kTileBytes;
-        const uint32_t ph = uint32_t(j) & 1u;
-        prof_mark<kProf>(p, rec, 2, j, 1);
-        for (int t = 0; t < 2; ++t) {
-          if (!(ok = mbar_wait(bar(kBarPFullA + t), ph, ctx, kStatusTimeoutP))) break;
-          prof_mark<kProf>(p, rec, 2, j, 2 + 3 * t);
-          tc_fence_after();
-          issue_pv_half(tmem + col_o(t), tmem + col_s(t) + 32, sv, 0, j > 0, 64);
-          mma_commit(bar(kBarODoneA + t));
-          if (!(ok = mbar_wait(bar(kBarPFullB + t), ph, ctx, kStatusTimeoutP))) break;
-          prof_mark<kProf>(p, rec, 2, j, 3 + 3 * t);
-          tc_fence_after();
-          issue_pv_half(tmem + col_o(t), tmem + col_s(t) + 32, sv, 1, true, 64);
-          mma_commit(bar(kBarODone + t));
-          if (t == 1) mma_commit(bar(kBarKVEmpty + it_v % kStages));
-          if (next) {
-            if (t == 0 && !(ok = wait_full(it_k))) break;  // overlaps the queued P*V work
-            issue_qk(tmem + col_s(t), sq + t * kTileBytes, sk);
-            mma_commit(bar(kBarSFull + t));
-            if (t == 1) mma_commit(bar(kBarKVEmpty + it_k % kStages));
-          }
-          prof_mark<kProf>(p, rec, 2, j, 4 + 3 * t);
-        }
-      }
-      mma_commit(bar(kBarDrain));
-      drain_wait(bar(kBarDrain), 0, p.status);
-    }
-  } else {
-    // ------------------------------------------------------------ softmax + epilogue (warps 0..15)
-    const int t = warp >> 3;            // Q tile
-    const int hq = (warp >> 2) & 1;     // which 16 lanes of the quadrant
-    const int quad = warp & 3;          // TMEM lane quadrant this warp may access
-    const int t0 = lane & 3, t1 = lane >> 2;
-    const uint32_t lane_off = uint32_t(32 * quad + 16 * hq) << 16;
-    const uint32_t tS = tmem + lane_off + col_s(t);
-    const uint32_t tO = tmem + lane_off + col_o(t);
-    const float c = p.scale_log2;
-    const int tail_valid = p.s_kv - (n_kv - 1) * kBlockN;
-    float m_run[2] = {-INFINITY, -INFINITY};
-    float l_part[2] = {0.f, 0.f};  // this thread's share of each row's sum
-    bool ok = !grid_aborted;
-    const bool rec = blockIdx.x == 0 && blockIdx.y == 0 && warp == 8 * t && lane == 0;
-
-    auto rescale = [&](const float (&m_new)[2], uint32_t o_bar, uint32_t o_parity, bool o_ready) -> bool {
-      const bool need0 = m_new[0] > m_run[0] + kRescaleThreshold;
-      const bool need1 = m_new[1] > m_run[1] + kRescaleThreshold;
-      if (!__any_sync(0xffffffffu, need0 || need1)) return true;
-      if (!o_ready && !__all_sync(0xffffffffu, mbar_wait(o_bar, o_parity, ctx, kStatusTimeoutO))) return false;
-      tc_fence_after();
-      const float f0 = need0 ? ex2_approx(m_run[0] - m_new[0]) : 1.0f;
-      const float f1 = need1 ? ex2_approx(m_run[1] - m_new[1]) : 1.0f;
-      if (need0) {
-        l_part[0] *= f0;
-        m_run[0] = m_new[0];
-      }
-      if (need1) {
-        l_part[1] *= f1;
-        m_run[1] = m_new[1];
-      }
-#pragma unroll 1
-      for (int c4 = 0; c4 < 4; ++c4) {
-        uint32_t o[16];
-        tmem_ld_16x256b_x4_wait(tO + c4 * 32, o);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * ((i & 2) ? f1 : f0));
-        tmem_st_16x256b_x4(tO + c4 * 32, o);
-      }
-      tmem_st_wait();
-      return true;
-    };
-
-    for (int j = 0; ok && j < n_kv; ++j) {
-      prof_mark<kProf>(p, rec, t, j, 0);
-      ok = __all_sync(0xffffffffu, mbar_wait(bar(kBarSFull + t), uint32_t(j) & 1u, ctx, kStatusTimeoutS));
-      if (!ok) break;
-      prof_mark<kProf>(p, rec, t, j, 1);
-      tc_fence_after();
-      if (kPingPong && (t == 1 || j > 0)) {
-        const uint32_t par = t == 0 ? uint32_t(j - 1) & 1u : uint32_t(j) & 1u;
-        ok = __all_sync(0xffffffffu, mbar_wait(bar(kBarTok + t), par, ctx, kStatusTimeoutS));
-        if (!ok) break;
-      }
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t sr[32];
-        tmem_ld_16x256b_x8_wait(tS + 64 * h, sr);
-        float s[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[i] = __uint_as_float(sr[i]);
-        if (j == n_kv - 1 && tail_valid < kBlockN) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int key = 64 * h + 8 * (i >> 2) + 2 * t0 + (i & 1);
-            if (key >= tail_valid) s[i] = -INFINITY;
-          }
-        }
-        if (h == 0) prof_mark<kProf>(p, rec, t, j, 2);
-        float mx0 = fmaxf(s[0], s[1]), mx1 = fmaxf(s[2], s[3]);
-#pragma unroll
-        for (int k = 1; k < 8; ++k) {
-          mx0 = fmaxf(mx0, fmaxf(s[4 * k], s[4 * k + 1]));
-          mx1 = fmaxf(mx1, fmaxf(s[4 * k + 2], s[4 * k + 3]));
-        }
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-        const float m_new[2] = {fmaxf(m_run[0], mx0 * c), fmaxf(m_run[1], mx1 * c)};
-        if (j == 0 && h == 0) {
-          m_run[0] = m_new[0];
-          m_run[1] = m_new[1];
-        } else if (h == 0) {
-          if (!(ok = rescale(m_new, 0, 0, true))) break;  // S_t(j) ready: earlier P*V retired
-        } else {
-          if (!(ok = rescale(m_new, bar(kBarODoneA + t), uint32_t(j) & 1u, false))) break;
-        }
-        prof_mark<kProf>(p, rec, t, j, 3 + 2 * h);
-        const float nm0 = -m_run[0], nm1 = -m_run[1];
-        float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
-        uint32_t pk[16];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          // FMA-pipe exp2 for the odd keys of selected repeats k: register slot (k, parity)
-          // holds key 64h + 8k + 2*t0 + parity for every t0, so the choice is a function of
-          // the key alone and each row's result stays independent of its position.
-          const bool poly = kEmu > 0 && (k % (kEmu > 1 ? kEmu / 2 : 1)) == (kEmu > 1 ? kEmu / 2 - 1 : 0);
-          const float e00 = ex2_approx(fmaf(s[4 * k], c, nm0));
-          const float e01 = poly ? ex2_poly(fmaf(s[4 * k + 1], c, nm0)) : ex2_approx(fmaf(s[4 * k + 1], c, nm0));
-          const float e10 = ex2_approx(fmaf(s[4 * k + 2], c, nm1));
-          const float e11 = poly ? ex2_poly(fmaf(s[4 * k + 3], c, nm1)) : ex2_approx(fmaf(s[4 * k + 3], c, nm1));
-          a0 += e00;
-          a1 += e01;
-          b0 += e10;
-          b1 += e11;
-          pk[2 * k] = pack_bf16x2(e00, e01);
-          pk[2 * k + 1] = pack_bf16x2(e10, e11);
-        }
-        if (kPingPong && h == 1) mbar_arrive(bar(kBarTok + (t ^ 1)));
-        l_part[0] += a0 + a1;
-        l_part[1] += b0 + b1;
-        tmem_st_16x128b_x8(tS + 32 + 64 * h, pk);
-        tmem_st_wait();
-        tc_fence_before();
-        mbar_arrive(bar(h == 0 ? kBarPFullA + t : kBarPFullB + t));
-        prof_mark<kProf>(p, rec, t, j, 4 + 2 * h);
-      }
-    }
-    if (ok) {
-      ok = __all_sync(0xffffffffu,
-                      mbar_wait(bar(kBarODone + t), uint32_t(n_kv - 1) & 1u, ctx, kStatusTimeoutO));
-    }
-    if (ok) {
-      tc_fence_after();
-      float l0 = l_part[0], l1 = l_part[1];
-      l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-      l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-      l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-      l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-      const float inv[2] = {1.0f / l0, 1.0f / l1};
-      __nv_bfloat16* dst[2];
-      bool valid[2];
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const int row = m0 + t * kBlockM + 32 * quad + 16 * hq + t1 + 8 * r;
-        valid[r] = row < p.s_q;
-        const long long rr = valid[r] ? row : 0;
-        dst[r] = p.o + (rr / p.o_rank_rows) * p.o_rank_stride + (long long)head * p.o_head_stride +
-                 (rr % p.o_rank_rows) * p.o_row_stride;
-      }
-#pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        uint32_t o[16];
-        tmem_ld_16x256b_x4_wait(tO + c4 * 32, o);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int col = 32 * c4 + 8 * k + 2 * t0;
-#pragma unroll
-          for (int r = 0; r < 2; ++r) {
-            const uint32_t w = pack_bf16x2(__uint_as_float(o[4 * k + 2 * r]) * inv[r],
-                                           __uint_as_float(o[4 * k + 2 * r + 1]) * inv[r]);
-            if (valid[r]) *reinterpret_cast<uint32_t*>(dst[r] + col) = w;
-          }
-        }
-      }
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == kWarpProducerV2) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
-}
-
-// ------------------------------------------------------------------ kernel v4: P through shared memory
-// The CTA shape of attn_fwd_kernel (two 128-row Q tiles, four softmax warps per tile, one query
-// row per thread), but P goes to shared memory -- one 16 KB SW128 buffer of 64 keys per Q tile,
-// reused by the two halves of a KV tile -- instead of S's TMEM columns. S_t is then free as soon
-// as the softmax has loaded it into registers, and the next S_t = Q_t K^T is issued right away,
-// under the softmax, instead of after P_t V: the per-tile chain shrinks to the softmax itself.
-// P*V reads P from shared memory (SS form). One MMA-issuing thread per Q tile (warps 1 and 3), so
-// one tile's hand-offs never wait behind the other's; K/V stages are released by both.
-constexpr int kStagesV4 = 4;
-constexpr uint32_t kOffQV4 = 0;
-constexpr uint32_t kOffPV4 = 2 * kTileBytes;                        // P_t: 16 KB each
-constexpr uint32_t kOffKVV4 = kOffPV4 + 2 * kHalfBytes;
-constexpr uint32_t kOffBarsV4 = kOffKVV4 + kStagesV4 * kTileBytes;  // 224 KB
-enum BarV4 : int {
-  kV4QFull = 0,
-  kV4KVFull = 1,
-  kV4KVEmpty = kV4KVFull + kStagesV4,  // released by both issuers
-  kV4SFull = kV4KVEmpty + kStagesV4,   // [t] S_t computed
-  kV4SFree = kV4SFull + 2,             // [t] S_t loaded into registers by the tile's 4 softmax warps
-  kV4PFullA = kV4SFree + 2,            // [t] P_t of keys 0..63 in shared memory
-  kV4PFullB = kV4PFullA + 2,           // [t] P_t of keys 64..127 in shared memory
-  kV4ODoneA = kV4PFullB + 2,           // [t] first-half P_t V retired (P buffer free again)
-  kV4ODone = kV4ODoneA + 2,            // [t] P_t V retired
-  kV4Drain = kV4ODone + 2,             // both issuers' MMAs retired
-  kV4Tok = kV4Drain + 1,               // [t] exp-phase token (kPingPong)
-  kV4NumBars = kV4Tok + 2
-};
-constexpr uint32_t kSmemBytesV4 = 1024 + kOffBarsV4 + kV4NumBars * 8 + 16;
-static_assert(kSmemBytesV4 <= 232448, "v4 shared memory exceeds the per-CTA limit");
-
-// O (+)= P V over 64 keys with P in shared memory: A = P (K-major, SW128, one 128-B row of 64
-// keys per query row, K steps +32 B), B = this half of V (MN-major) as in issue_pv_half.
-__device__ __forceinline__ void issue_pv_smem_half(uint32_t d_tmem, uint32_t p_base, uint32_t v_base, int half,
-                                                   bool accumulate) {
-  constexpr uint32_t idesc = idesc_bf16_f32(128, 128, 0, 1);
-  const uint64_t ad = smem_desc_sw128(p_base, 16, 1024);
-  const uint64_t bd = smem_desc_sw128(v_base + uint32_t(half) * 4u * 2048u, kHalfBytes, 1024);
-  const uint32_t alo = uint32_t(ad), ahi = uint32_t(ad >> 32), blo = uint32_t(bd), bhi = uint32_t(bd >> 32);
-#define H3_PVS_STEP(KK) \
-  "add.u32 la, %1, " #KK "*2;\n\t add.u32 lb, %3, " #KK "*128;\n\t" \
-  "mov.b64 da, {la, %2};\n\t mov.b64 db, {lb, %4};\n\t" \
-  "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %5, pt;\n\t"
-  asm volatile(
-      "{\n\t.reg .pred pf, pt;\n\t.reg .b32 la, lb;\n\t.reg .b64 da, db;\n\t"
-      "setp.ne.b32 pf, %6, 0;\n\t setp.eq.b32 pt, %6, %6;\n\t"
-      "mov.b64 da, {%1, %2};\n\t mov.b64 db, {%3, %4};\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %5, pf;\n\t"
-      H3_PVS_STEP(1) H3_PVS_STEP(2) H3_PVS_STEP(3)
-      "}\n" ::"r"(d_tmem), "r"(alo), "r"(ahi), "r"(blo), "r"(bhi), "r"(idesc), "r"(accumulate ? 1u : 0u)
-      : "memory");
-#undef H3_PVS_STEP
-}
-
-__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
-}
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
-// kPingPong: the two tiles' softmax warpgroups take turns for each 64-key exp phase (a token
-// passed through two mbarriers: tile 0's n-th phase follows tile 1's (n-1)-th, tile 1's n-th
-// follows tile 0's n-th), so one exponentiates while the other loads, reduces and stores.
-template <bool kProf, bool kPingPong>
-__global__ void __launch_bounds__(kThreads, 1)
-    attn_fwd_v4_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
-                       const __grid_constant__ CUtensorMap tmap_v, const Params p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const uint32_t sbase = smem_u32(smem);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBarsV4);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kV4NumBars);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  auto bar = [&](int i) { return smem_u32(&bars[i]); };
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int head = blockIdx.y;
-  const int m0 = blockIdx.x * kRowsPerCta;
-  const int n_kv = p.n_kv_tiles;
-
-  if (threadIdx.x == 0) {
-    mbar_init(bar(kV4QFull), 1);
-    for (int s = 0; s < kStagesV4; ++s) {
-      mbar_init(bar(kV4KVFull + s), 1);
-      mbar_init(bar(kV4KVEmpty + s), 2);
-    }
-    for (int t = 0; t < 2; ++t) {
-      mbar_init(bar(kV4SFull + t), 1);
-      mbar_init(bar(kV4SFree + t), 4);
-      mbar_init(bar(kV4PFullA + t), 4);
-      mbar_init(bar(kV4PFullB + t), 4);
-      mbar_init(bar(kV4ODoneA + t), 1);
-      mbar_init(bar(kV4ODone + t), 1);
-    }
-    mbar_init(bar(kV4Drain), 2);
-    mbar_init(bar(kV4Tok + 0), 4);
-    mbar_init(bar(kV4Tok + 1), 4);
-    *abort_flag = (*reinterpret_cast<volatile int*>(p.status) != 0) ? 1 : 0;
-    fence_mbar_init();
-  }
-  if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tmap_q);
-    tma_prefetch_desc(&tmap_k);
-    tma_prefetch_desc(&tmap_v);
-  }
-  if (warp == 2) {
-    tmem_alloc(smem_u32(tmem_slot), 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  const WaitCtx ctx{abort_flag, p.status};
-  const bool grid_aborted = *abort_flag != 0;
-
-  if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer: Q, then K_0, V_0, K_1, V_1, ...
-    if (lane == 0 && !grid_aborted) {
-      const uint32_t sq = sbase + kOffQV4;
-      const uint32_t skv = sbase + kOffKVV4;
-      mbar_expect_tx(bar(kV4QFull), 2 * kTileBytes);
-      for (int t = 0; t < 2; ++t)
-        for (int hh = 0; hh < 2; ++hh)
-          tma_load_3d(sq + t * kTileBytes + hh * kHalfBytes, &tmap_q, bar(kV4QFull), hh * 64, m0 + t * kBlockM, head);
-      int it = 0;
-      for (int j = 0; j < n_kv; ++j) {
-        bool ok = true;
-        for (int kv = 0; kv < 2; ++kv, ++it) {
-          const int st = it % kStagesV4;
-          if (!mbar_wait(bar(kV4KVEmpty + st), (uint32_t(it / kStagesV4) & 1u) ^ 1u, ctx, kStatusTimeoutKV)) {
-            ok = false;
-            break;
-          }
-          const CUtensorMap* m = kv ? &tmap_v : &tmap_k;
-          mbar_expect_tx(bar(kV4KVFull + st), kTileBytes);
-          tma_load_3d(skv + st * kTileBytes, m, bar(kV4KVFull + st), 0, j * kBlockN, head);
-          tma_load_3d(skv + st * kTileBytes + kHalfBytes, m, bar(kV4KVFull + st), 64, j * kBlockN, head);
-        }
-        if (!ok) break;
-      }
-      drain_wait(bar(kV4QFull), 0, p.status);
-      for (int st = 0; st < kStagesV4; ++st) {
-        const int cnt = it / kStagesV4 + (st < it % kStagesV4 ? 1 : 0);
-        if (cnt > 0) drain_wait(bar(kV4KVFull + st), uint32_t(cnt - 1) & 1u, p.status);
-      }
-    }
-  } else if (warp == 1 || warp == 3) {
-    // ------------------------------------------------------------ MMA issuer of Q tile t
-    // Per iteration j: S_t(j+1) = Q_t K_{j+1}^T as soon as the softmax has taken S_t(j), then
-    // O_t += P_t V_j in two 64-key halves as the softmax hands them over.
-    if (lane == 0 && !grid_aborted) {
-      const int t = warp == 1 ? 0 : 1;
-      const uint32_t sq = sbase + kOffQV4 + t * kTileBytes;
-      const uint32_t sp = sbase + kOffPV4 + t * kHalfBytes;
-      const uint32_t skv = sbase + kOffKVV4;
-      const bool rec = t == 0 && blockIdx.x == 0 && blockIdx.y == 0;
-      auto wait_full = [&](int it) -> bool {
-        return mbar_wait(bar(kV4KVFull + it % kStagesV4), uint32_t(it / kStagesV4) & 1u, ctx, kStatusTimeoutKV);
-      };
-      bool ok = mbar_wait(bar(kV4QFull), 0, ctx, kStatusTimeoutQ) && wait_full(0);
-      if (ok) {
-        issue_qk(tmem + col_s(t), sq, skv);
-        mma_commit(bar(kV4SFull + t));
-        mma_commit(bar(kV4KVEmpty + 0));
-      }
-      for (int j = 0; ok && j < n_kv; ++j) {
-        prof_mark<kProf>(p, rec, 2, j, 0);
-        const uint32_t ph = uint32_t(j) & 1u;
-        const int it_v = 2 * j + 1, it_k = 2 * j + 2;
-        if (j + 1 < n_kv) {
-          if (!(ok = mbar_wait(bar(kV4SFree + t), ph, ctx, kStatusTimeoutP))) break;
-          prof_mark<kProf>(p, rec, 2, j, 1);
-          if (!(ok = wait_full(it_k))) break;
-          tc_fence_after();
-          issue_qk(tmem + col_s(t), sq, skv + (it_k % kStagesV4) * kTileBytes);
-          mma_commit(bar(kV4SFull + t));
-          mma_commit(bar(kV4KVEmpty + it_k % kStagesV4));
-          prof_mark<kProf>(p, rec, 2, j, 2);
-        }
-        if (!(ok = wait_full(it_v))) break;
-        const uint32_t sv = skv + (it_v % kStagesV4) * kTileBytes;
-        if (!(ok = mbar_wait(bar(kV4PFullA + t), ph, ctx, kStatusTimeoutP))) break;
-        prof_mark<kProf>(p, rec, 2, j, 3);
-        tc_fence_after();
-        issue_pv_smem_half(tmem + col_o(t), sp, sv, 0, j > 0);
-        mma_commit(bar(kV4ODoneA + t));
-        prof_mark<kProf>(p, rec, 2, j, 4);
-        if (!(ok = mbar_wait(bar(kV4PFullB + t), ph, ctx, kStatusTimeoutP))) break;
-        prof_mark<kProf>(p, rec, 2, j, 5);
-        tc_fence_after();
-        issue_pv_smem_half(tmem + col_o(t), sp, sv, 1, true);
-        mma_commit(bar(kV4ODone + t));
-        mma_commit(bar(kV4KVEmpty + it_v % kStagesV4));
-        prof_mark<kProf>(p, rec, 2, j, 6);
-      }
-      mma_commit(bar(kV4Drain));
-      drain_wait(bar(kV4Drain), 0, p.status);
-    }
-  } else if (warp >= 4) {
-    // ------------------------------------------------------------ softmax + epilogue
-    const int t = (warp - 4) >> 2;  // Q tile
-    const int quad = warp & 3;      // TMEM lane quadrant this warp may access
-    const int r = quad * 32 + lane;  // row within the tile
-    const uint32_t lane_off = uint32_t(quad * 32) << 16;
-    const uint32_t tS = tmem + lane_off + col_s(t);
-    const uint32_t tO = tmem + lane_off + col_o(t);
-    const uint32_t p_row = sbase + kOffPV4 + t * kHalfBytes + uint32_t(r) * 128u;  // SW128: chunk c at c ^ (r & 7)
-    const uint32_t swz = uint32_t(r & 7);
-    const float c = p.scale_log2;
-    const int tail_valid = p.s_kv - (n_kv - 1) * kBlockN;
-    float m_run = -INFINITY;
-    float l_run = 0.f;
-    bool ok = !grid_aborted;
-    const bool rec = blockIdx.x == 0 && blockIdx.y == 0 && quad == 0 && lane == 0;
-
-    for (int j = 0; ok && j < n_kv; ++j) {
-      prof_mark<kProf>(p, rec, t, j, 0);
-      ok = __all_sync(0xffffffffu, mbar_wait(bar(kV4SFull + t), uint32_t(j) & 1u, ctx, kStatusTimeoutS));
-      if (!ok) break;
-      prof_mark<kProf>(p, rec, t, j, 1);
-      tc_fence_after();
-      uint32_t sa[64], sb[64];
-      tmem_ld64_wait(tS, sa);
-      tmem_ld64_wait(tS + 64, sb);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(kV4SFree + t));  // S_t may be overwritten by the next Q_t K^T
-      float s[128];
-#pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        s[i] = __uint_as_float(sa[i]);
-        s[64 + i] = __uint_as_float(sb[i]);
-      }
-      if (j == n_kv - 1 && tail_valid < kBlockN) {
-#pragma unroll
-        for (int i = 0; i < 128; ++i)
-          if (i >= tail_valid) s[i] = -INFINITY;
-      }
-      prof_mark<kProf>(p, rec, t, j, 2);
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        float mx0 = s[64 * h], mx1 = s[64 * h + 1], mx2 = s[64 * h + 2], mx3 = s[64 * h + 3];
-#pragma unroll
-        for (int i = 4; i < 64; i += 4) {
-          mx0 = fmaxf(mx0, s[64 * h + i]);
-          mx1 = fmaxf(mx1, s[64 * h + i + 1]);
-          mx2 = fmaxf(mx2, s[64 * h + i + 2]);
-          mx3 = fmaxf(mx3, s[64 * h + i + 3]);
-        }
-        const float m_new = fmaxf(m_run, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * c);
-        // The P*V this half must follow: h = 0 -> all of P(j-1) (o_done, phase j-1), which also
-        // frees the P buffer; h = 1 -> the first half of P(j) (o_done_a, phase j).
-        const uint32_t o_bar = bar(h == 0 ? kV4ODone + t : kV4ODoneA + t);
-        const uint32_t o_par = h == 0 ? uint32_t(j - 1) & 1u : uint32_t(j) & 1u;
-        const bool first = j == 0 && h == 0;
-        if (first) {
-          m_run = m_new;  // O is not written before P(0) V (accumulate off)
-        } else {
-          const bool need = m_new > m_run + kRescaleThreshold;
-          if (__any_sync(0xffffffffu, need)) {
-            if (!(ok = __all_sync(0xffffffffu, mbar_wait(o_bar, o_par, ctx, kStatusTimeoutO)))) break;
-            tc_fence_after();
-            const float f = need ? ex2_approx(m_run - m_new) : 1.0f;
-            if (need) {
-              l_run *= f;
-              m_run = m_new;
-            }
-#pragma unroll 1
-            for (int c16 = 0; c16 < 8; ++c16) {
-              uint32_t o[16];
-              tmem_ld16_wait(tO + c16 * 16, o);
-#pragma unroll
-              for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
-              tmem_st16(tO + c16 * 16, o);
-            }
-            tmem_st_wait();
-          }
-        }
-        const int phase = 2 * j + h;  // this warpgroup's exp phase count
-        if (kPingPong && (t == 1 || phase > 0)) {
-          const uint32_t tp = t == 0 ? uint32_t(phase - 1) & 1u : uint32_t(phase) & 1u;
-          if (!(ok = __all_sync(0xffffffffu, mbar_wait(bar(kV4Tok + t), tp, ctx, kStatusTimeoutS)))) break;
-        }
-        const float neg_m = -m_run;
-        float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
-        uint32_t pk[32];
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const int e = 64 * h + 2 * i;
-          const float e0 = ex2_approx(fmaf(s[e], c, neg_m));
-          const float e1 = ex2_approx(fmaf(s[e + 1], c, neg_m));
-          const float e2 = ex2_approx(fmaf(s[e + 2], c, neg_m));
-          const float e3 = ex2_approx(fmaf(s[e + 3], c, neg_m));
-          l0 += e0;
-          l1 += e1;
-          l2 += e2;
-          l3 += e3;
-          pk[i] = pack_bf16x2(e0, e1);
-          pk[i + 1] = pack_bf16x2(e2, e3);
-        }
-        if (kPingPong) {
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar(kV4Tok + (t ^ 1)));  // hand the exp phase over
-        }
-        l_run += (l0 + l1) + (l2 + l3);
-        // the P buffer is free once the P*V that read it retired
-        if (!first && !(ok = __all_sync(0xffffffffu, mbar_wait(o_bar, o_par, ctx, kStatusTimeoutO)))) break;
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch)
-          st_shared_v4(p_row + ((uint32_t(ch) ^ swz) << 4), pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2],
-                       pk[4 * ch + 3]);
-        fence_proxy_async_smem();
-        tc_fence_before();  // the rescale's TMEM stores, if any, precede the hand-off too
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(h == 0 ? kV4PFullA + t : kV4PFullB + t));
-        prof_mark<kProf>(p, rec, t, j, 3 + h);
-      }
-    }
-    if (ok) {
-      ok = __all_sync(0xffffffffu, mbar_wait(bar(kV4ODone + t), uint32_t(n_kv - 1) & 1u, ctx, kStatusTimeoutO));
-    }
-    if (ok) {
-      tc_fence_after();
-      const float inv = 1.0f / l_run;
-      const int row = m0 + t * kBlockM + r;
-      const bool valid = row < p.s_q;
-      const long long rr = valid ? row : 0;
-      __nv_bfloat16* dst = p.o + (rr / p.o_rank_rows) * p.o_rank_stride + (long long)head * p.o_head_stride +
-                           (rr % p.o_rank_rows) * p.o_row_stride;
-#pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        uint32_t o[32];
-        tmem_ld32_wait(tO + c4 * 32, o);
-        uint32_t w[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          w[i] = pack_bf16x2(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
-        if (valid) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + c4 * 32);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
-        }
-      }
     }
   }
 
@@ -1386,6 +680,56 @@ __global__ void __launch_bounds__(128, 1)
   }
 }
 
+// Bounded-wait known-answer kernel: the path every kernel here takes when a wait runs out,
+// exercised on purpose. Thread 0 starts a TMA load of one 128x128 tile (a copy in flight), then
+// waits with the caller's limit on an mbarrier that nothing ever arrives on; warps 1-3 wait for
+// thread 0's hand-off, which never comes. When the limit passes, the waiters record
+// kStatusTimeoutKat and raise the CTA's abort flag (which also releases the other waiters),
+// thread 0 drains its copy, and the CTA frees its TMEM and returns: the GPU stays usable and
+// the host reads the code from the status word.
+__global__ void __launch_bounds__(128, 1)
+    kat_wait_kernel(const __grid_constant__ CUtensorMap tmap, int* status, unsigned long long limit_ns) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTileBytes);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5;
+  const uint32_t b_full = smem_u32(&bars[0]), b_never = smem_u32(&bars[1]), b_handoff = smem_u32(&bars[2]);
+  if (threadIdx.x == 0) {
+    mbar_init(b_full, 1);
+    mbar_init(b_never, 1);
+    mbar_init(b_handoff, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(tmem_slot), 32);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  WaitCtx ctx{abort_flag, status};
+  ctx.limit_ns = limit_ns;
+  if (threadIdx.x == 0) {
+    mbar_expect_tx(b_full, kTileBytes);
+    for (int hh = 0; hh < 2; ++hh) tma_load_3d(sbase + hh * kHalfBytes, &tmap, b_full, hh * 64, 0, 0);
+    if (mbar_wait(b_never, 0, ctx, kStatusTimeoutKat)) mbar_arrive(b_handoff);
+    drain_wait(b_full, 0, status);
+  } else if (warp != 0) {
+    mbar_wait(b_handoff, 0, ctx, kStatusTimeoutKat);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 32);
+  }
+}
+
 // ---------------------------------------------------------------- host side
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -1422,33 +766,13 @@ static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 using namespace h3::attn;
 
-template <bool kPingPong, int kEmu, bool kProf = false, bool kDual = false, bool kSpec = false>
+template <bool kPingPong, int kEmu, bool kProf = false, bool kDual = false>
 static int launch_variant(dim3 grid, cudaStream_t st, const CUtensorMap& tq, const CUtensorMap& tk,
                           const CUtensorMap& tv, const Params& p) {
-  auto* kern = attn_fwd_kernel<kPingPong, kEmu, kProf, kDual, kSpec>;
+  auto* kern = attn_fwd_kernel<kPingPong, kEmu, kProf, kDual>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) != cudaSuccess)
     return H3_ERR_LAUNCH;
   kern<<<grid, kThreads, kSmemBytes, st>>>(tq, tk, tv, p);
-  return cudaGetLastError() == cudaSuccess ? H3_OK : H3_ERR_LAUNCH;
-}
-
-template <bool kPingPong, int kEmu, bool kProf = false>
-static int launch_v2(dim3 grid, cudaStream_t st, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                     const Params& p) {
-  auto* kern = attn_fwd_v2_kernel<kPingPong, kEmu, kProf>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) != cudaSuccess)
-    return H3_ERR_LAUNCH;
-  kern<<<grid, kThreadsV2, kSmemBytes, st>>>(tq, tk, tv, p);
-  return cudaGetLastError() == cudaSuccess ? H3_OK : H3_ERR_LAUNCH;
-}
-
-template <bool kProf, bool kPingPong>
-static int launch_v4(dim3 grid, cudaStream_t st, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                     const Params& p) {
-  auto* kern = attn_fwd_v4_kernel<kProf, kPingPong>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytesV4) != cudaSuccess)
-    return H3_ERR_LAUNCH;
-  kern<<<grid, kThreads, kSmemBytesV4, st>>>(tq, tk, tv, p);
   return cudaGetLastError() == cudaSuccess ? H3_OK : H3_ERR_LAUNCH;
 }
 
@@ -1476,11 +800,6 @@ static int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, i
 
   const long long qhs = n_heads > 1 ? q_head_stride : s_q * q_row_stride;
   const long long kvhs = n_heads > 1 ? kv_head_stride : s_kv * kv_row_stride;
-  if ((variant >= 13 && variant <= 15) || variant == 20)
-    return h3::pair::launch_attn(q, k, v, o, n_heads, s_q, s_kv, qhs, q_row_stride, kvhs, kv_row_stride, o_rank_rows,
-                                 o_rank_stride, o_head_stride, o_row_stride,
-                                 (float)((double)softmax_scale * 1.4426950408889634), status, variant, prof, prof_iters,
-                                 reinterpret_cast<cudaStream_t>(stream));
   CUtensorMap tq, tk, tv;
   int rc;
   if ((rc = make_head_map(&tq, q, s_q, n_heads, q_row_stride, qhs)) != H3_OK) return rc;
@@ -1511,35 +830,20 @@ static int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, i
       case 1: return launch_variant<true, 0, true>(grid, st, tq, tk, tv, p);
       case 2: return launch_variant<true, 4, true>(grid, st, tq, tk, tv, p);
       case 3: return launch_variant<true, 8, true>(grid, st, tq, tk, tv, p);
-      case 5: return launch_v2<false, 0, true>(grid, st, tq, tk, tv, p);
-      case 6: return launch_v2<true, 0, true>(grid, st, tq, tk, tv, p);
-      case 8: return launch_v2<false, 4, true>(grid, st, tq, tk, tv, p);
       case 10: return launch_variant<false, 0, true, true>(grid, st, tq, tk, tv, p);
       case 11: return launch_variant<true, 0, true, true>(grid, st, tq, tk, tv, p);
-      case 16: return launch_v4<true, false>(grid, st, tq, tk, tv, p);
-      case 17: return launch_v4<true, true>(grid, st, tq, tk, tv, p);
-      case 18: return launch_variant<false, 0, true, false, true>(grid, st, tq, tk, tv, p);
       default: return H3_ERR_UNSUPPORTED;
     }
   }
   switch (variant) {
-    case 5: return launch_v2<false, 0>(grid, st, tq, tk, tv, p);
-    case 6: return launch_v2<true, 0>(grid, st, tq, tk, tv, p);
-    case 7: return launch_v2<false, 8>(grid, st, tq, tk, tv, p);
-    case 8: return launch_v2<false, 4>(grid, st, tq, tk, tv, p);
-    case 9: return launch_v2<false, 2>(grid, st, tq, tk, tv, p);
-    case 10: return launch_variant<false, 0, false, true>(grid, st, tq, tk, tv, p);
-    case 11: return launch_variant<true, 0, false, true>(grid, st, tq, tk, tv, p);
-    case 12: return launch_variant<false, 8, false, true>(grid, st, tq, tk, tv, p);
     case 0: return launch_variant<false, 0>(grid, st, tq, tk, tv, p);
     case 1: return launch_variant<true, 0>(grid, st, tq, tk, tv, p);
     case 2: return launch_variant<true, 4>(grid, st, tq, tk, tv, p);
     case 3: return launch_variant<true, 8>(grid, st, tq, tk, tv, p);
     case 4: return launch_variant<true, 2>(grid, st, tq, tk, tv, p);
-    case 16: return launch_v4<false, false>(grid, st, tq, tk, tv, p);
-    case 17: return launch_v4<false, true>(grid, st, tq, tk, tv, p);
-    case 18: return launch_variant<false, 0, false, false, true>(grid, st, tq, tk, tv, p);
-    case 19: return launch_variant<false, 0, false, true, true>(grid, st, tq, tk, tv, p);
+    case 10: return launch_variant<false, 0, false, true>(grid, st, tq, tk, tv, p);
+    case 11: return launch_variant<true, 0, false, true>(grid, st, tq, tk, tv, p);
+    case 12: return launch_variant<false, 8, false, true>(grid, st, tq, tk, tv, p);
     default: return H3_ERR_UNSUPPORTED;
   }
 }
@@ -1576,12 +880,14 @@ extern "C" int h3_attn_fwd(const void* q, const void* k, const void* v, void* o,
 }
 
 extern "C" int h3_attn_fwd_peer(const void* q, const void* k, const void* v, void* o_local, const uint64_t* o_peer,
-                                int64_t n_heads, int64_t s_q, int64_t s_kv, int64_t q_head_stride,
+                                int64_t n_ranks, int64_t n_heads, int64_t s_q, int64_t s_kv, int64_t q_head_stride,
                                 int64_t q_row_stride, int64_t kv_head_stride, int64_t kv_row_stride,
                                 int64_t o_rank_rows, int64_t o_head_stride, int64_t o_row_stride, float softmax_scale,
                                 int32_t* status, void* stream) {
   if (!o_peer) return H3_ERR_NULL;
   if (reinterpret_cast<uintptr_t>(o_peer) & 7u) return H3_ERR_ALIGN;
+  // the epilogue indexes o_peer[row / o_rank_rows]: the table must cover every query row
+  if (n_ranks < 1 || n_ranks > 65536 || o_rank_rows < 1 || s_q > n_ranks * o_rank_rows) return H3_ERR_SHAPE;
   if (kDefaultVariant != 0) return H3_ERR_UNSUPPORTED;  // the peer epilogue lives in attn_fwd_kernel
   return attn_fwd_impl(q, k, v, o_local, n_heads, s_q, s_kv, q_head_stride, q_row_stride, kv_head_stride,
                        kv_row_stride, o_rank_rows, 0, o_head_stride, o_row_stride, softmax_scale, status,
@@ -1613,5 +919,20 @@ extern "C" int h3_tile_kat_pv(const void* p_in, const void* v, float* o_out, int
     return H3_ERR_LAUNCH;
   kat_pv_kernel<<<1, 128, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const __nv_bfloat16*>(p_in), tv, o_out, status);
+  return cudaGetLastError() == cudaSuccess ? H3_OK : H3_ERR_LAUNCH;
+}
+
+extern "C" int h3_wait_kat(const void* tile, int64_t limit_ns, int32_t* status, void* stream) {
+  if (!tile || !status) return H3_ERR_NULL;
+  if (!aligned16(tile) || (reinterpret_cast<uintptr_t>(status) & 3u)) return H3_ERR_ALIGN;
+  if (limit_ns < 1000 || limit_ns > 10ll * 1000 * 1000 * 1000) return H3_ERR_SHAPE;
+  CUtensorMap tm;
+  int rc;
+  if ((rc = make_head_map(&tm, tile, 128, 1, 128, 128 * 128)) != H3_OK) return rc;
+  const int smem = 1024 + kTileBytes + 64;
+  if (cudaFuncSetAttribute(kat_wait_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return H3_ERR_LAUNCH;
+  kat_wait_kernel<<<1, 128, smem, reinterpret_cast<cudaStream_t>(stream)>>>(tm, status,
+                                                                            (unsigned long long)limit_ns);
   return cudaGetLastError() == cudaSuccess ? H3_OK : H3_ERR_LAUNCH;
 }

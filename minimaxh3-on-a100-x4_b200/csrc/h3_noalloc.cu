@@ -22,6 +22,8 @@
 // Calls whose work overlaps on the GPU (other streams, other host threads) race on the
 // array. The call waits for its stream to drain so it can return the kernel's status.
 #include <atomic>
+#include <cmath>
+#include <cstdint>
 
 #include "h3_ptx.cuh"
 #include "h3attn.h"
@@ -53,11 +55,23 @@ int scratch_for_current_device(unsigned char** out) {
 
 }  // namespace
 
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
 extern "C" int h3_attn_layer_noalloc(const void* qkv, int64_t qkv_row_stride, const float* rope,
                                      int64_t rope_row_stride, const void* q_weight, const void* k_weight, float eps,
                                      void* o, int64_t s, int64_t n_heads, float softmax_scale, void* stream) {
+  // Every argument is checked here, before anything is enqueued: a call that one of the two
+  // kernels would reject must not leave the other half-done in the shared array.
   if (!qkv || !o) return H3_ERR_NULL;
-  if (s < 1 || n_heads < 1) return H3_ERR_SHAPE;
+  if (!aligned16(qkv) || !aligned16(o) || (rope && !aligned16(rope)) || (q_weight && !aligned16(q_weight)) ||
+      (k_weight && !aligned16(k_weight)))
+    return H3_ERR_ALIGN;
+  if (s < 1 || n_heads < 1 || n_heads > 65535 || s > (int64_t(1) << 31) - 512) return H3_ERR_SHAPE;
+  // q, k and v are the three column blocks of one row: the row must hold all three
+  if (qkv_row_stride < 3 * n_heads * 128 || (qkv_row_stride % 8) ||
+      (rope && (rope_row_stride < 256 || (rope_row_stride % 4))))
+    return H3_ERR_STRIDE;
+  if (!(eps >= 0.f) || !(softmax_scale > 0.f) || !std::isfinite(softmax_scale)) return H3_ERR_SHAPE;
   const int64_t head_elems = s * 128;
   if (n_heads > (int64_t)(kPackedMaxBytes / (3 * 2 * (size_t)head_elems))) return H3_ERR_SCRATCH_LIMIT;
   unsigned char* base = nullptr;

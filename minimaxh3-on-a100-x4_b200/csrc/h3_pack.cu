@@ -204,7 +204,7 @@ extern "C" int h3_qknorm_rope_pack(const void* q, const void* k, const void* v, 
       (k_weight && !aligned16(k_weight)))
     return H3_ERR_ALIGN;
   if (s_l < 1 || n_heads < 1 || heads_per_rank < 1 || n_heads % heads_per_rank) return H3_ERR_SHAPE;
-  if (s_l * 3 * n_heads > (1ll << 40)) return H3_ERR_SHAPE;
+  if (s_l > (1ll << 31) || n_heads > 65535 || s_l * 3 * n_heads > (1ll << 40)) return H3_ERR_SHAPE;
   if (in_row_stride < n_heads * 128 || (in_row_stride % 8) || (out_rank_stride % 8) || (out_head_stride % 8) ||
       (rope && (rope_row_stride < 256 || (rope_row_stride % 4))))
     return H3_ERR_STRIDE;
@@ -224,15 +224,18 @@ extern "C" int h3_qknorm_rope_pack(const void* q, const void* k, const void* v, 
 extern "C" int h3_qknorm_rope_pack_peer(const void* q, const void* k, const void* v, int64_t in_row_stride,
                                         const float* rope, int64_t rope_row_stride, const void* q_weight,
                                         const void* k_weight, float eps, const uint64_t* rank_base,
-                                        int64_t tensor_stride, int64_t head_stride, int64_t row_offset, int64_t s_l,
-                                        int64_t n_heads, int64_t heads_per_rank, void* stream) {
+                                        int64_t n_ranks, int64_t tensor_stride, int64_t head_stride,
+                                        int64_t row_offset, int64_t s_l, int64_t n_heads, int64_t heads_per_rank,
+                                        void* stream) {
   if (!q || !k || !v || !rank_base) return H3_ERR_NULL;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || (rope && !aligned16(rope)) ||
       (q_weight && !aligned16(q_weight)) || (k_weight && !aligned16(k_weight)) ||
       (reinterpret_cast<uintptr_t>(rank_base) & 7u))
     return H3_ERR_ALIGN;
   if (s_l < 1 || n_heads < 1 || heads_per_rank < 1 || n_heads % heads_per_rank || row_offset < 0) return H3_ERR_SHAPE;
-  if (s_l * 3 * n_heads > (1ll << 40)) return H3_ERR_SHAPE;
+  if (s_l > (1ll << 31) || n_heads > 65535 || s_l * 3 * n_heads > (1ll << 40)) return H3_ERR_SHAPE;
+  // the kernel indexes rank_base[head / heads_per_rank]: the table must cover every destination
+  if (n_ranks < 1 || n_heads / heads_per_rank > n_ranks) return H3_ERR_SHAPE;
   if (in_row_stride < n_heads * 128 || (in_row_stride % 8) || (tensor_stride % 8) || (head_stride % 8) ||
       tensor_stride < 0 || head_stride < 0 || (rope && (rope_row_stride < 256 || (rope_row_stride % 4))))
     return H3_ERR_STRIDE;

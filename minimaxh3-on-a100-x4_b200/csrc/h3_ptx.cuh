@@ -2,8 +2,8 @@
 // mbarriers with bounded waits, TMA tile loads (no cluster multicast anywhere),
 // tcgen05 tensor-memory allocation, MMA issue/commit, and TMEM loads/stores.
 //
-// Every wait here is bounded: after H3_WAIT_LIMIT_NS of polling (measured with
-// %globaltimer) the waiter records an error code in the caller's device status
+// Every wait here is bounded: after WaitCtx::limit_ns of polling (H3_WAIT_LIMIT_NS unless
+// a caller passes its own; measured with %globaltimer) the waiter records an error code in the caller's device status
 // word, raises the CTA's abort flag and returns false, so the kernel can wind down
 // and return instead of hanging the GPU.
 #pragma once
@@ -66,10 +66,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Shared state a CTA uses to give up cleanly: `abort` lives in shared memory,
-// `status` is the caller's device status word (also read as a grid-wide abort).
+// `status` is the caller's device status word (also read as a grid-wide abort),
+// `limit_ns` how long one wait may poll before it gives up.
 struct WaitCtx {
   volatile int* abort;
   int* status;
+  unsigned long long limit_ns = H3_WAIT_LIMIT_NS;
 };
 
 // Bounded wait on phase `parity` of `bar`. Returns false when the CTA must abort.
@@ -84,7 +86,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const W
         *ctx.abort = 1;
         return false;
       }
-      if (globaltimer_ns() - t0 > H3_WAIT_LIMIT_NS) {
+      if (globaltimer_ns() - t0 > ctx.limit_ns) {
         atomicCAS(ctx.status, 0, code);
         *ctx.abort = 1;
         return false;
@@ -351,7 +353,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
         *ctx.abort = 1;
         return false;
       }
-      if (globaltimer_ns() - t0 > H3_WAIT_LIMIT_NS) {
+      if (globaltimer_ns() - t0 > ctx.limit_ns) {
         atomicCAS(ctx.status, 0, code);
         *ctx.abort = 1;
         return false;

@@ -33,6 +33,8 @@ _ERRORS = {
     -7: "driver entry point unavailable",
     -8: "unsupported configuration",
     -9: "a CUDA runtime call failed",
+    -10: "the call needs more than the no-alloc entry point's static scratch",
+    -11: "a kernel gave up waiting (bounded-wait timeout)",
 }
 STATUS_NAMES = {
     0: "ok", 1: "timeout waiting for Q tiles", 2: "timeout in the K/V ring", 3: "timeout waiting for S",
@@ -71,6 +73,8 @@ def lib() -> ctypes.CDLL:
         L.h3_tile_kat_qk.restype = ctypes.c_int
         L.h3_tile_kat_pv.argtypes = [vp, vp, vp, i32p, vp]
         L.h3_tile_kat_pv.restype = ctypes.c_int
+        L.h3_wait_kat.argtypes = [vp, i64, i32p, vp]
+        L.h3_wait_kat.restype = ctypes.c_int
         for name in ("h3_tile_kat_pair_qk", "h3_tile_kat_pair_pv"):
             getattr(L, name).argtypes = [vp, vp, vp, i32p, vp]
             getattr(L, name).restype = ctypes.c_int
@@ -82,9 +86,9 @@ def lib() -> ctypes.CDLL:
         L.h3_gated_residual.argtypes = [vp, i64, vp, i64, vp, i64, vp, vp, i64, i64, i64, vp]
         L.h3_gated_residual.restype = ctypes.c_int
         L.h3_qknorm_rope_pack_peer.argtypes = [vp, vp, vp, i64, vp, i64, vp, vp, ctypes.c_float, vp, i64, i64, i64,
-                                               i64, i64, i64, vp]
+                                               i64, i64, i64, i64, vp]
         L.h3_qknorm_rope_pack_peer.restype = ctypes.c_int
-        L.h3_attn_fwd_peer.argtypes = [vp] * 5 + [i64] * 10 + [ctypes.c_float, i32p, vp]
+        L.h3_attn_fwd_peer.argtypes = [vp] * 5 + [i64] * 11 + [ctypes.c_float, i32p, vp]
         L.h3_attn_fwd_peer.restype = ctypes.c_int
         L.h3_status_read.argtypes = [i32p, vp]
         L.h3_status_read.restype = ctypes.c_int
@@ -196,7 +200,7 @@ def qknorm_rope_pack_peer(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, rop
     if tuple(rank_base.shape) != (world,) or not rank_base.is_contiguous():
         raise H3Error("rank_base must be a contiguous int64 [world] device tensor")
     rc = lib().h3_qknorm_rope_pack_peer(q2.data_ptr(), k2.data_ptr(), v2.data_ptr(), q2.stride(0), rope_ptr,
-                                        rope_stride, wptr[0], wptr[1], float(eps), rank_base.data_ptr(),
+                                        rope_stride, wptr[0], wptr[1], float(eps), rank_base.data_ptr(), world,
                                         tensor_stride, head_stride, row_offset, sl, H, H // world, _stream())
     _check(rc, "h3_qknorm_rope_pack_peer")
 
@@ -219,8 +223,8 @@ def attention_peer(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o_local: t
         raise H3Error("o_peer must hold one address per destination rank")
     s_kv = k.shape[1] if s_kv is None else int(s_kv)
     scale = 1.0 / math.sqrt(D) if scale is None else float(scale)
-    rc = lib().h3_attn_fwd_peer(q.data_ptr(), k.data_ptr(), v.data_ptr(), o_local.data_ptr(), o_peer.data_ptr(), H,
-                                sq, s_kv, q.stride(0), q.stride(1), k.stride(0), k.stride(1), rank_rows, head_stride,
+    rc = lib().h3_attn_fwd_peer(q.data_ptr(), k.data_ptr(), v.data_ptr(), o_local.data_ptr(), o_peer.data_ptr(),
+                                o_peer.shape[0], H, sq, s_kv, q.stride(0), q.stride(1), k.stride(0), k.stride(1), rank_rows, head_stride,
                                 row_stride, scale, status_word(q.device).data_ptr(), _stream())
     _check(rc, "h3_attn_fwd_peer")
 
@@ -482,3 +486,14 @@ def tile_kat_pair_pv(p: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
     _check(lib().h3_tile_kat_pair_pv(p.data_ptr(), v.data_ptr(), o.data_ptr(), status_word(p.device).data_ptr(),
                                      _stream()), "h3_tile_kat_pair_pv")
     return o
+
+
+def wait_kat(tile: torch.Tensor, limit_ns: int) -> None:
+    """Launch the bounded-wait KAT: one CTA loads `tile` [128, 128] bf16 by TMA, then waits up to
+    limit_ns on a barrier nothing completes, reports H3_STATUS_TIMEOUT_KAT in the status word and
+    returns. Read the outcome with check_status() (which raises on it)."""
+    _cuda(tile, "tile")
+    if tuple(tile.shape) != (128, 128) or not tile.is_contiguous():
+        raise H3Error("tile must be a contiguous [128, 128] bf16 tensor")
+    _check(lib().h3_wait_kat(tile.data_ptr(), int(limit_ns), status_word(tile.device).data_ptr(), _stream()),
+           "h3_wait_kat")

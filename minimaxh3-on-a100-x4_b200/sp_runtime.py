@@ -42,7 +42,10 @@ There is no CPU path: the kernels live in h3attn (libh3attn.so) and raise if it 
 """
 from __future__ import annotations
 
+import contextlib
 import os
+import time
+import warnings
 from datetime import timedelta
 
 import torch
@@ -74,43 +77,57 @@ def ops():
     return _ops
 
 
-# ---- optional per-op timing (SP_TIMING=1): CUDA-event category accumulators ----
+# ---- per-category timing of run_blocks (SP_TIMING=1) ----
+# The categories are the reference's (sp_runtime.py:31-58, consumed by harness/sp_full_step.py:66):
+# norm_mod, qkv, a2a_fwd, fa2_local, a2a_inv, out_proj, residual, ffn, gather.
 _TIMING = os.environ.get("SP_TIMING") == "1"
-_acc = {}
-_last = {}
+CATEGORIES = ("norm_mod", "qkv", "a2a_fwd", "fa2_local", "a2a_inv", "out_proj", "residual", "ffn", "gather")
+_timeline = None   # the _Timeline of the run_blocks call in progress, when timing
+_last_totals = {}  # category -> ms of the last finished run_blocks call
 
 
-class _tr:
-    def __init__(self, cat):
-        self.cat = cat
+class _Timeline:
+    """Spans of one run_blocks call. On the GPU each span is a pair of CUDA events recorded on the
+    current stream, so totals are device time and reading them needs one synchronisation at the end
+    of the call; on host tensors (the CPU gloo tests) the host clock brackets the span."""
 
-    def __enter__(self):
-        if _TIMING:
-            self.s = torch.cuda.Event(enable_timing=True)
-            self.e = torch.cuda.Event(enable_timing=True)
-            self.s.record()
-        return self
+    def __init__(self, on_gpu: bool):
+        self.on_gpu = on_gpu
+        self.marks = []  # (category, start, end)
 
-    def __exit__(self, *a):
-        if _TIMING:
-            self.e.record()
-            _acc.setdefault(self.cat, []).append((self.s, self.e))
-        return False
+    def _stamp(self):
+        if self.on_gpu:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            return ev
+        return time.perf_counter()
+
+    @contextlib.contextmanager
+    def span(self, cat: str):
+        t0 = self._stamp()
+        try:
+            yield
+        finally:
+            self.marks.append((cat, t0, self._stamp()))
+
+    def totals(self) -> dict:
+        if self.on_gpu:
+            torch.cuda.synchronize()
+        out = {}
+        for cat, a, b in self.marks:
+            ms = a.elapsed_time(b) if self.on_gpu else (b - a) * 1e3
+            out[cat] = out.get(cat, 0.0) + ms
+        return out
 
 
-def _finalize_timing():
-    global _acc
-    if not _TIMING:
-        return
-    torch.cuda.synchronize()
-    _last.clear()
-    for cat, pairs in _acc.items():
-        _last[cat] = sum(s.elapsed_time(e) for s, e in pairs)
-    _acc = {}
+def _span(cat: str):
+    """Context manager booking the enclosed work under `cat` while a timed run_blocks is running."""
+    return _timeline.span(cat) if _timeline is not None else contextlib.nullcontext()
 
 
 def get_timing():
-    return dict(_last)
+    """Per-category ms of the last run_blocks call (empty unless SP_TIMING=1)."""
+    return dict(_last_totals)
 
 
 def init(timeout_s: float | None = None):
@@ -172,13 +189,38 @@ def _norm_inputs(self, x, rope_freqs):
     return rope, qw, kw
 
 
+_STRICT = os.environ.get("SP_STRICT") == "1"
+_fallbacks_seen = set()
+
+
+def _host_fallback(what: str, why: str) -> None:
+    """A projection or block the library's kernels cannot take runs on the host module's own torch
+    ops. Said once per kind on rank 0; with SP_STRICT=1 it is an error instead."""
+    if _STRICT:
+        raise RuntimeError(f"sp_runtime: {what} would fall back to the host module's ops ({why}); SP_STRICT=1")
+    key = (what, why)
+    if key not in _fallbacks_seen:
+        _fallbacks_seen.add(key)
+        if RANK == 0:
+            warnings.warn(f"sp_runtime: {what} runs on the host module's ops ({why})", RuntimeWarning, stacklevel=3)
+
+
 def _gemm_weight(lin, x):
     """The weight of a bias-free bf16 Linear that the projection GEMM takes for input x, or None
-    (then the host module's own op runs, as in the reference)."""
+    (then the host module's own op runs, as in the reference, and the fallback is reported)."""
     w = getattr(lin, "weight", None)
-    if not isinstance(w, torch.Tensor) or getattr(lin, "bias", None) is not None:
-        return None
-    if w.dtype != torch.bfloat16 or w.dim() != 2 or x.dtype != torch.bfloat16 or w.device != x.device:
+    why = None
+    if not isinstance(w, torch.Tensor):
+        why = "no weight tensor"
+    elif getattr(lin, "bias", None) is not None:
+        why = "the linear has a bias"
+    elif w.dtype != torch.bfloat16 or x.dtype != torch.bfloat16:
+        why = f"dtype {w.dtype} weight / {x.dtype} input (bf16 needed)"
+    elif w.dim() != 2 or w.device != x.device:
+        why = "weight shape or device"
+    if why is not None:
+        if x.is_cuda:
+            _host_fallback("a projection", why)
         return None
     return w
 
@@ -199,25 +241,25 @@ def _sp_attn_forward(self, x, rope_freqs=None, transformer_options={}):
     O = ops()
     s = x.shape[0]
     H, D, W = self.heads, self.head_dim, WORLD
-    with _tr("qkv"):
+    with _span("qkv"):
         w_qkv = _gemm_weight(self.qkv_proj, x)
         qkv = O.linear(x, w_qkv) if w_qkv is not None else self.qkv_proj(x)
         q, k, v = qkv.split(H * D, dim=-1)
         rope, qw, kw = _norm_inputs(self, x, rope_freqs)
         send = O.qknorm_rope_pack(q, k, v, rope, qw, kw, self.q_norm.eps, W)  # [W, 3, H/W, s, D]
-    with _tr("a2a_fwd"):
+    with _span("a2a_fwd"):
         qkvh = O.seq_to_head_unpack(_exchange(send)) if W > 1 else send[0]  # [3, H/W, W*s, D]
-    with _tr("fa2_local"):
+    with _span("fa2_local"):
         S_pad = W * s
         s_kv = _SP_REAL_S if (_SP_REAL_S is not None and _SP_REAL_S < S_pad) else S_pad
         if W > 1:
             o_send = O.attention(qkvh[0], qkvh[1], qkvh[2], s_kv=s_kv, layout="send", world=W)
         else:
             o = O.attention(qkvh[0], qkvh[1], qkvh[2], s_kv=s_kv, layout="token")
-    with _tr("a2a_inv"):
+    with _span("a2a_inv"):
         if W > 1:
             o_recv = _exchange(o_send)  # [W, H/W, s, D] == [H, s, D]
-    with _tr("out_proj"):
+    with _span("out_proj"):
         w_out = _gemm_weight(self.out_proj, x)
         if W > 1:
             o_heads = o_recv.view(H, s, D)
@@ -312,7 +354,7 @@ def _sp_attn_forward_heads(self, x, rope_freqs=None, transformer_options={}):
     s = x.shape[0]
     H, D, W = self.heads, self.head_dim, WORLD
     hl = H // W
-    with _tr("qkv"):
+    with _span("qkv"):
         w_qkv = _gemm_weight(self.qkv_proj, x)
         qkv = O.linear(x, w_qkv) if w_qkv is not None else self.qkv_proj(x)
         q, k, v = qkv.split(H * D, dim=-1)
@@ -322,7 +364,7 @@ def _sp_attn_forward_heads(self, x, rope_freqs=None, transformer_options={}):
     s_kv = _SP_REAL_S if (_SP_REAL_S is not None and _SP_REAL_S < S_pad) else S_pad
     default = torch.cuda.current_stream()
     o_heads = torch.empty((W, hl, s, D), dtype=x.dtype, device=x.device)  # == [H, s, D], head g = src*hl + h
-    with _tr("fa2_local"):
+    with _span("fa2_local"):
         _comm_stream.wait_stream(default)
         _side_stream.wait_stream(default)
         send.record_stream(_comm_stream)
@@ -348,7 +390,7 @@ def _sp_attn_forward_heads(self, x, rope_freqs=None, transformer_options={}):
                 o_heads[:, h].copy_(_exchange(o_send).view(W, s, D))
         default.wait_stream(_side_stream)
         default.wait_stream(_comm_stream)
-    with _tr("out_proj"):
+    with _span("out_proj"):
         w_out = _gemm_weight(self.out_proj, x)
         o_hsd = o_heads.view(H, s, D)
         return O.linear(o_hsd, w_out) if w_out is not None else self.out_proj(O.head_to_seq_unpack(o_hsd))
@@ -417,21 +459,21 @@ def _sp_attn_forward_peer(self, x, rope_freqs=None, transformer_options={}):
     buf = _peer_buffers(s, H, D, x.device)[0]
     S_pad = W * s
     s_kv = _SP_REAL_S if (_SP_REAL_S is not None and _SP_REAL_S < S_pad) else S_pad
-    with _tr("qkv"):
+    with _span("qkv"):
         w_qkv = _gemm_weight(self.qkv_proj, x)
         qkv = O.linear(x, w_qkv) if w_qkv is not None else self.qkv_proj(x)
         q, k, v = qkv.split(H * D, dim=-1)
         rope, qw, kw = _norm_inputs(self, x, rope_freqs)
         O.qknorm_rope_pack_peer(q, k, v, rope, qw, kw, self.q_norm.eps, W, buf["qkv_ptrs"], hl * S_pad * D,
                                 S_pad * D, RANK * s)
-    with _tr("a2a_fwd"):
+    with _span("a2a_fwd"):
         _peer_barrier(buf["flag"])  # every rank's q/k/v rows have landed
-    with _tr("fa2_local"):
+    with _span("fa2_local"):
         qkvh = buf["qkv"]
         O.attention_peer(qkvh[0], qkvh[1], qkvh[2], buf["o"], buf["o_ptrs"], s, D, H * D, s_kv=s_kv)
-    with _tr("a2a_inv"):
+    with _span("a2a_inv"):
         _peer_barrier(buf["flag"])  # every rank's output rows for this rank have landed
-    with _tr("out_proj"):
+    with _span("out_proj"):
         w_out = _gemm_weight(self.out_proj, x)
         return O.linear(buf["o"], w_out) if w_out is not None else self.out_proj(buf["o"].clone())
 
@@ -445,51 +487,64 @@ def _shard_segments(segs, lo, hi):
     return out
 
 
-def _sp_block_timed(self, x, t_emb, mod_segments, rope_freqs, transformer_options={}):
-    """Timing-instrumented replica of DiTBlock.forward (ref :203-218)."""
+def _host_block_timed(self, x, t_emb, mod_segments, rope_freqs, transformer_options={}):
+    """The host DiTBlock.forward, op for op, with each step booked under its timing category
+    (used instead of the block's own forward only while SP_TIMING=1 and only for blocks the fused
+    kernels cannot take; the patched attention books its own sub-steps)."""
     MM = _MODULE
-    with _tr("norm_mod"):
-        shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = self.adaln_proj(t_emb)
-        h = MM._mod_scale_shift(self.norm1(x), shift_msa, scale_msa, mod_segments)
-    a = self.attn(h, rope_freqs=rope_freqs, transformer_options=transformer_options)
-    with _tr("residual"):
-        x = MM._mod_gate(x, gate_msa, a, mod_segments)
-    with _tr("norm_mod"):
-        h = MM._mod_scale_shift(self.norm2(x), shift_mlp, scale_mlp, mod_segments)
-    with _tr("ffn"):
-        m = self.mlp(h)
-    with _tr("residual"):
-        return MM._mod_gate(x, gate_mlp, m, mod_segments)
+    with _span("norm_mod"):
+        mods = self.adaln_proj(t_emb)
+        shift1, scale1, gate1, shift2, scale2, gate2 = mods
+        h = MM._mod_scale_shift(self.norm1(x), shift1, scale1, mod_segments)
+    attn_out = self.attn(h, rope_freqs=rope_freqs, transformer_options=transformer_options)
+    with _span("residual"):
+        x = MM._mod_gate(x, gate1, attn_out, mod_segments)
+    with _span("norm_mod"):
+        h = MM._mod_scale_shift(self.norm2(x), shift2, scale2, mod_segments)
+    with _span("ffn"):
+        ffn_out = self.mlp(h)
+    with _span("residual"):
+        return MM._mod_gate(x, gate2, ffn_out, mod_segments)
 
 
 def _fusable(blk, x) -> bool:
     """The block's norms are affine-free LayerNorms over the hidden width and x is bf16 on the GPU,
-    so the fused modulation kernels reproduce the host ops (else the host block runs)."""
-    if not (x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2 and x.shape[1] % 8 == 0 and x.shape[1] <= 8192):
+    so the fused modulation kernels reproduce the host ops (else the host block runs, reported once)."""
+    if not x.is_cuda:
         return False
-    for n in (getattr(blk, "norm1", None), getattr(blk, "norm2", None)):
-        if not isinstance(n, torch.nn.LayerNorm) or n.weight is not None or n.bias is not None:
-            return False
-        if tuple(n.normalized_shape) != (x.shape[1],):
-            return False
+    why = None
+    if not (x.dtype == torch.bfloat16 and x.dim() == 2 and x.shape[1] % 8 == 0 and x.shape[1] <= 8192):
+        why = f"activations {x.dtype} {tuple(x.shape)} (bf16, hidden <= 8192 and a multiple of 8 needed)"
+    else:
+        for n in (getattr(blk, "norm1", None), getattr(blk, "norm2", None)):
+            if not isinstance(n, torch.nn.LayerNorm) or n.weight is not None or n.bias is not None:
+                why = "a norm that is not an affine-free LayerNorm"
+            elif tuple(n.normalized_shape) != (x.shape[1],):
+                why = "a norm over another width"
+    if why is not None:
+        _host_fallback("the AdaLN modulation of a block", why)
+        return False
     return True
 
 
 def _sp_block(self, x, t_emb, seg_row, rope_freqs, transformer_options={}):
-    """The host block in the timed replica's op order (ref :203-218) with the AdaLN modulation and
-    gated residuals on the library's kernels, three passes over [rows, hidden]: norm1 + modulation;
-    attention residual + norm2 + modulation; FFN residual."""
+    """The host block's op order (DiTBlock.forward, as the reference's timed replica walks it at
+    sp_runtime.py:203-218) with the AdaLN modulation and gated residuals on the library's kernels:
+    three passes over [rows, hidden]: norm1 + modulation; attention residual + norm2 + modulation;
+    FFN residual."""
     O = ops()
-    with _tr("norm_mod"):
+    with _span("norm_mod"):
         shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = self.adaln_proj(t_emb)
         h = O.norm_modulate(x, shift_msa, scale_msa, seg_row, self.norm1.eps)
     a = self.attn(h, rope_freqs=rope_freqs, transformer_options=transformer_options)
-    with _tr("residual"):
+    # one pass does the attention residual, norm2 and its modulation: booked as norm_mod (its bulk);
+    # residual then holds the closing gated residual only
+    with _span("norm_mod"):
         x1 = torch.empty_like(x)
         h = O.norm_modulate(x, shift_mlp, scale_mlp, seg_row, self.norm2.eps, y=a, gate=gate_msa, x_out=x1)
-    with _tr("ffn"):
+    with _span("ffn"):
         m = self.mlp(h)
-    with _tr("residual"):
+    with _span("residual"):
         return O.gated_residual(x1, m, gate_mlp, seg_row)
 
 
@@ -502,26 +557,33 @@ def _gather_rows(h_loc: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def _shard_bounds(S: int, world: int, rank: int) -> tuple[int, int, int]:
+    """(S_pad, lo, hi): the sequence is padded to the next multiple of world and rank holds rows
+    [lo, hi) of the padded sequence (the reference's pad rule, sp_runtime.py:224-239)."""
+    rows = -(-S // world)
+    return rows * world, rank * rows, (rank + 1) * rows
+
+
 def _sp_run_blocks(self, h, t_emb, mod_segments, rope_freqs, transformer_options={}):
-    global _SP_ACTIVE, _SP_REAL_S
+    global _SP_ACTIVE, _SP_REAL_S, _timeline
     S = h.shape[0]
-    # Exact uneven-S padding: pad rows go at the tail, outside every modulation segment,
-    # and their key positions are excluded inside attention via _SP_REAL_S.
-    S_pad = ((S + WORLD - 1) // WORLD) * WORLD
-    P = S_pad - S
-    if P > 0:
-        h = torch.cat([h, h.new_zeros(P, h.shape[1])], dim=0)
+    S_pad, lo, hi = _shard_bounds(S, WORLD, RANK)
+    # Pad rows sit after the last token: they belong to no modulation segment (scale, shift and
+    # gate leave them alone), their keys are cut off inside attention (_SP_REAL_S), and the
+    # all-gather's tail drops them again.
+    h_loc = h[lo:min(hi, S)]
+    rope_loc = rope_freqs[:, lo:min(hi, S)] if rope_freqs is not None else None
+    if hi > S:
+        h_loc = torch.cat([h_loc, h.new_zeros(hi - max(lo, S), h.shape[1])], dim=0)
         if rope_freqs is not None:
-            pad_shape = (rope_freqs.shape[0], P) + tuple(rope_freqs.shape[2:])
-            rope_freqs = torch.cat([rope_freqs, rope_freqs.new_zeros(pad_shape)], dim=1)
-    Sl = S_pad // WORLD
-    lo, hi = RANK * Sl, (RANK + 1) * Sl
-    h_loc = h[lo:hi].contiguous()
-    rope_loc = rope_freqs[:, lo:hi].contiguous() if rope_freqs is not None else None
+            tail = rope_freqs.new_zeros((rope_freqs.shape[0], hi - max(lo, S)) + tuple(rope_freqs.shape[2:]))
+            rope_loc = torch.cat([rope_loc, tail], dim=1)
+    h_loc = h_loc.contiguous()
+    rope_loc = rope_loc.contiguous() if rope_loc is not None else None
     segs_loc = _shard_segments(mod_segments, lo, hi)
-    blkfn = _sp_block_timed if _TIMING else None
-    _SP_ACTIVE = True
-    _SP_REAL_S = S
+    host_block = _host_block_timed if _TIMING else None
+    _timeline = _Timeline(h_loc.is_cuda) if _TIMING else None
+    _SP_ACTIVE, _SP_REAL_S = True, S
     seg_row = None
     try:
         for blk in self.blocks:
@@ -529,17 +591,24 @@ def _sp_run_blocks(self, h, t_emb, mod_segments, rope_freqs, transformer_options
                 if seg_row is None:
                     seg_row = ops().segment_rows(segs_loc, h_loc.shape[0], h_loc.device)
                 h_loc = _sp_block(blk, h_loc, t_emb, seg_row, rope_loc, transformer_options=transformer_options)
-            elif blkfn is not None:
-                h_loc = blkfn(blk, h_loc, t_emb, segs_loc, rope_loc, transformer_options=transformer_options)
+            elif host_block is not None:
+                h_loc = host_block(blk, h_loc, t_emb, segs_loc, rope_loc, transformer_options=transformer_options)
             else:
                 h_loc = blk(h_loc, t_emb, segs_loc, rope_loc, transformer_options=transformer_options)
-        with _tr("gather"):
+        with _span("gather"):
             out = _gather_rows(h_loc) if WORLD > 1 else h_loc
     finally:
-        _SP_ACTIVE = False
-        _SP_REAL_S = None
-    _finalize_timing()
-    return out[:S] if P > 0 else out
+        _SP_ACTIVE, _SP_REAL_S = False, None
+        timeline, _timeline = _timeline, None
+    if timeline is not None:
+        _last_totals.clear()
+        _last_totals.update(timeline.totals())
+    # A kernel that gave up a bounded wait leaves a code in the device status word and its output
+    # rows unwritten: raise here rather than hand back such activations (one sync per call).
+    check = getattr(ops(), "check_status", None)
+    if check is not None and out.is_cuda:
+        check(out.device)
+    return out[:S] if S_pad > S else out
 
 
 def install(module=None):

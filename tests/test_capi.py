@@ -111,7 +111,7 @@ def test_gemm_rejects_bad_arguments_before_launch(L):
 def test_peer_entry_points_reject_bad_arguments_before_launch(L):
     p, st = ctypes.c_void_p(0x1000), ctypes.c_void_p(0x2000)
     # pack: q, k, v [10][4*128], 2 ranks, table of 2 addresses
-    ok = [p, p, p, 4 * 128, None, 0, None, None, ctypes.c_float(1e-6), p, 20 * 128, 10 * 128, 0, 10, 4, 2, None]
+    ok = [p, p, p, 4 * 128, None, 0, None, None, ctypes.c_float(1e-6), p, 2, 20 * 128, 10 * 128, 0, 10, 4, 2, None]
     bad = list(ok)
     bad[9] = None
     assert L.h3_qknorm_rope_pack_peer(*bad) == -1                 # no address table
@@ -119,13 +119,17 @@ def test_peer_entry_points_reject_bad_arguments_before_launch(L):
     bad[9] = ctypes.c_void_p(0x1004)
     assert L.h3_qknorm_rope_pack_peer(*bad) == -2                 # table not 8-byte aligned
     bad = list(ok)
-    bad[15] = 3
+    bad[16] = 3
     assert L.h3_qknorm_rope_pack_peer(*bad) == -3                 # heads not divisible into ranks
     bad = list(ok)
-    bad[10] = 20 * 128 + 4
+    bad[10] = 1
+    assert L.h3_qknorm_rope_pack_peer(*bad) == -3                 # table shorter than the destination ranks
+    bad = list(ok)
+    bad[11] = 20 * 128 + 4
     assert L.h3_qknorm_rope_pack_peer(*bad) == -4                 # tensor stride not a multiple of 8
     # attention: [2][128][128] q/k/v, two destination ranks of 64 rows
-    a = [p, p, p, p, p, 2, 128, 128, 128 * 128, 128, 128 * 128, 128, 64, 128, 256, ctypes.c_float(0.088), st, None]
+    a = [p, p, p, p, p, 2, 2, 128, 128, 128 * 128, 128, 128 * 128, 128, 64, 128, 256, ctypes.c_float(0.088), st,
+         None]
     bad = list(a)
     bad[4] = None
     assert L.h3_attn_fwd_peer(*bad) == -1                         # no address table
@@ -133,8 +137,45 @@ def test_peer_entry_points_reject_bad_arguments_before_launch(L):
     bad[4] = ctypes.c_void_p(0x1004)
     assert L.h3_attn_fwd_peer(*bad) == -2
     bad = list(a)
-    bad[6] = 0
+    bad[7] = 0
     assert L.h3_attn_fwd_peer(*bad) == -3                         # no query rows
+    bad = list(a)
+    bad[5] = 1
+    assert L.h3_attn_fwd_peer(*bad) == -3                         # 128 rows, one table entry of 64 rows
+
+
+def test_noalloc_rejects_bad_arguments_before_any_work(L):
+    """Every argument of h3_attn_layer_noalloc is checked before anything is enqueued, so a
+    rejected call never leaves the shared static array half-written."""
+    L.h3_attn_layer_noalloc.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64,
+                                        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float, ctypes.c_void_p,
+                                        ctypes.c_int64, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p]
+    p = ctypes.c_void_p(0x1000)
+    ok = [p, 3 * 4 * 128, None, 0, None, None, ctypes.c_float(1e-6), p, 100, 4, ctypes.c_float(0.088), None]
+    bad = list(ok)
+    bad[0] = None
+    assert L.h3_attn_layer_noalloc(*bad) == -1
+    bad = list(ok)
+    bad[7] = ctypes.c_void_p(0x1008)
+    assert L.h3_attn_layer_noalloc(*bad) == -2                    # output not 16-byte aligned
+    bad = list(ok)
+    bad[1] = 4 * 128                                              # row holds q only: k, v reads would overrun
+    assert L.h3_attn_layer_noalloc(*bad) == -4
+    bad = list(ok)
+    bad[1] = 3 * 4 * 128 - 8
+    assert L.h3_attn_layer_noalloc(*bad) == -4
+    bad = list(ok)
+    bad[9], bad[8], bad[1] = 70000, 1, 3 * 70000 * 128
+    assert L.h3_attn_layer_noalloc(*bad) == -3                    # more heads than the attention grid takes
+    bad = list(ok)
+    bad[8] = 1 << 60                                              # absurd length: rejected, no overflow
+    assert L.h3_attn_layer_noalloc(*bad) == -3
+    bad = list(ok)
+    bad[10] = ctypes.c_float(0.0)
+    assert L.h3_attn_layer_noalloc(*bad) == -3                    # scale must be positive
+    bad = list(ok)
+    bad[8], bad[9], bad[1] = 1561, 56, 3 * 56 * 128
+    assert L.h3_attn_layer_noalloc(*bad) == -10                   # beyond the static scratch
 
 
 def test_no_cpu_path():

@@ -82,3 +82,51 @@ def test_peer_layout_offsets():
         base = me * hl * D
         off = base + h * D + (i % sl) * (H * D)
         assert off == o[i % sl, (me * hl + h) * D:].storage_offset()
+
+
+def test_host_fallback_reported_once_or_refused_in_strict_mode():
+    import warnings
+
+    import sp_runtime
+    sp_runtime._fallbacks_seen.clear()
+    old = sp_runtime._STRICT
+    try:
+        sp_runtime._STRICT = False
+        with warnings.catch_warnings(record=True) as w:
+            warnings.simplefilter("always")
+            sp_runtime._host_fallback("a projection", "the linear has a bias")
+            sp_runtime._host_fallback("a projection", "the linear has a bias")
+        assert len([x for x in w if "host module's ops" in str(x.message)]) == 1
+        sp_runtime._STRICT = True
+        with pytest.raises(RuntimeError, match="SP_STRICT"):
+            sp_runtime._host_fallback("a projection", "the linear has a bias")
+    finally:
+        sp_runtime._STRICT = old
+        sp_runtime._fallbacks_seen.clear()
+
+
+@pytest.mark.parametrize("S,world", [(42000, 8), (41999, 8), (67, 4), (3, 4), (64, 1)])
+def test_shard_bounds_follow_the_pad_rule(S, world):
+    """S_pad = ceil(S / world) * world; rank r holds rows [r * S_pad/world, (r+1) * S_pad/world)."""
+    import sp_runtime
+    spans = [sp_runtime._shard_bounds(S, world, r) for r in range(world)]
+    S_pad = spans[0][0]
+    assert S_pad % world == 0 and S <= S_pad < S + world
+    assert spans[0][1] == 0 and spans[-1][2] == S_pad
+    assert all(a[2] == b[1] for a, b in zip(spans, spans[1:]))
+    assert len({hi - lo for _, lo, hi in spans}) == 1
+
+
+def test_timeline_books_host_spans_by_category():
+    import time
+
+    import sp_runtime
+    tl = sp_runtime._Timeline(on_gpu=False)
+    with tl.span("qkv"):
+        time.sleep(0.01)
+    with tl.span("qkv"):
+        pass
+    with tl.span("gather"):
+        pass
+    tot = tl.totals()
+    assert set(tot) == {"qkv", "gather"} and tot["qkv"] >= 9.0 and tot["gather"] >= 0.0

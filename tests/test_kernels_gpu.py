@@ -186,10 +186,10 @@ def test_bad_arguments_rejected(cuda_dev):
         h3attn.attention(q, q, q, layout="send", world=3)
 
 
-@pytest.mark.parametrize("variant", [0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15, 16, 17, 18, 19, 20])
+@pytest.mark.parametrize("variant", [0, 1, 2, 3, 4, 10, 11, 12])
 def test_attention_variants_vs_oracle(cuda_dev, variant):
-    """Every kernel schedule meets the tolerance; the ping-pong schedule without FMA-pipe
-    exponentials is bit-identical to the free-running one (scheduling only)."""
+    """Every kernel schedule meets the tolerance; the schedules that only reorder work (ping-pong
+    token, one MMA issuer per Q tile) are bit-identical to the default."""
     import h3attn
     H, S_real, S_pad = 2, 1001, 1004
     q, k, v = _inputs(21, H, S_pad, cuda_dev)
@@ -199,11 +199,7 @@ def test_attention_variants_vs_oracle(cuda_dev, variant):
     ref = O.attention(q, k, v, s_kv=S_real)
     err = np.abs(o.float().cpu().numpy() - ref)
     assert err.max() < MAX_ABS and err.mean() < MEAN_ABS, (err.max(), err.mean())
-    if variant == 1:
-        assert torch.equal(o, h3attn.attention(qd, kd, vd, s_kv=S_real, variant=0))
-    if variant == 6:
-        assert torch.equal(o, h3attn.attention(qd, kd, vd, s_kv=S_real, variant=5))
-    if variant in (10, 11, 16, 17, 18, 19):  # same arithmetic in another schedule
+    if variant in (1, 10, 11):  # same arithmetic in another schedule
         assert torch.equal(o, h3attn.attention(qd, kd, vd, s_kv=S_real, variant=0))
     # every variant keeps rows independent of each other: a row subset is bit-identical
     sub = h3attn.attention(qd[:, 129:700], kd, vd, s_kv=S_real, variant=variant)
@@ -211,25 +207,9 @@ def test_attention_variants_vs_oracle(cuda_dev, variant):
     assert torch.equal(sub, o[:, 129:700])
 
 
-@pytest.mark.parametrize("H,S", [(2, 1), (2, 100), (2, 128), (2, 129), (2, 256), (2, 257), (3, 300), (2, 513),
-                                 (1, 1000)])
-@pytest.mark.parametrize("variant", [13, 14, 15, 16, 17, 18, 20])
-def test_pair_kernel_vs_oracle(cuda_dev, H, S, variant):
-    """The SM-pair kernels (variants 13-15) and the P-in-shared-memory kernel (16) over ragged sizes: a pair whose second CTA has no rows
-    (S <= 128 + 256k), a lone key tile, odd tails; rows past S are never written."""
+def test_removed_variants_rejected(cuda_dev):
     import h3attn
-    q, k, v = _inputs(31 + S, H, S, cuda_dev)
-    qd, kd, vd = (_bf16(a, cuda_dev) for a in (q, k, v))
-    out = torch.full((H, S + 8, 128), 7.0, dtype=torch.bfloat16, device=cuda_dev)
-    rc = h3attn.lib().h3_attn_fwd_variant(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), out.data_ptr(), H, S, S,
-                                          qd.stride(0), qd.stride(1), kd.stride(0), kd.stride(1), S, 0,
-                                          (S + 8) * 128, 128, 128 ** -0.5, h3attn.status_word(cuda_dev).data_ptr(),
-                                          variant, torch.cuda.current_stream().cuda_stream)
-    assert rc == 0, rc
-    torch.cuda.synchronize()
-    h3attn.check_status()
-    o = out[:, :S]
-    ref = O.attention(q, k, v)
-    err = np.abs(o.float().cpu().numpy() - ref)
-    assert err.max() < MAX_ABS and err.mean() < MEAN_ABS, (err.max(), err.mean())
-    assert bool((out[:, S:] == 7.0).all())
+    q = torch.zeros(1, 128, 128, dtype=torch.bfloat16, device=cuda_dev)
+    for variant in (5, 13, 20, 99):
+        with pytest.raises(h3attn.H3Error):
+            h3attn.attention(q, q, q, variant=variant)

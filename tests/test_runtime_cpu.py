@@ -36,10 +36,12 @@ def _setup_env(rank, world, port):
             sys.path.insert(0, p)
 
 
-def _seam_worker(rank, world, port, out_dir, cases, overlap):
+def _seam_worker(rank, world, port, out_dir, cases, overlap, timing=False):
     _setup_env(rank, world, port)
     if overlap:
         os.environ["SP_OVERLAP"] = "1"
+    if timing:
+        os.environ["SP_TIMING"] = "1"
     import sp_runtime
     from oracle import cpu_ops
     from golden.make_golden import seam_setup
@@ -47,11 +49,12 @@ def _seam_worker(rank, world, port, out_dir, cases, overlap):
     sp_runtime._ops = cpu_ops
     sp_runtime.init(timeout_s=60)
     sp_runtime.install()
-    res = {}
+    res, timing = {}, {}
     for S in cases:
         model, h, t_emb, segs, rope = seam_setup(S)
         with torch.no_grad():
             res[S] = MM.MiniMaxH3Model.run_blocks(model, h.clone(), t_emb, segs, rope, {}).numpy()
+        timing[S] = sp_runtime.get_timing()
     # the reference API a2a helpers
     H, Sl = 8, 5
     g = torch.Generator().manual_seed(7)
@@ -60,18 +63,32 @@ def _seam_worker(rank, world, port, out_dir, cases, overlap):
     z = sp_runtime.a2a_head_to_seq(y.clone(), world, H)
     sp_runtime.uninstall()
     np.savez(os.path.join(out_dir, f"r{rank}.npz"), y=y.numpy(), z=z.numpy(),
-             **{f"seam_{S}": v for S, v in res.items()})
+             **{f"seam_{S}": v for S, v in res.items()},
+             **{f"timing_{S}": np.array(sorted(t.items()), dtype=object) for S, t in timing.items()})
     if torch.distributed.is_initialized():
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
 
 
-def _run(world, cases, overlap=False):
+def _run(world, cases, overlap=False, timing=False):
     import torch.multiprocessing as mp
     with tempfile.TemporaryDirectory() as d:
-        mp.start_processes(_seam_worker, args=(world, _free_port(), d, cases, overlap), nprocs=world,
+        mp.start_processes(_seam_worker, args=(world, _free_port(), d, cases, overlap, timing), nprocs=world,
                            start_method="spawn")
-        return [dict(np.load(os.path.join(d, f"r{r}.npz"))) for r in range(world)]
+        return [dict(np.load(os.path.join(d, f"r{r}.npz"), allow_pickle=True)) for r in range(world)]
+
+
+def test_sp_timing_reports_the_reference_categories():
+    """SP_TIMING=1: get_timing() after run_blocks holds exactly the categories that
+    harness/sp_full_step.py:66 reads, each a non-negative ms figure, and the output is unchanged."""
+    outs = _run(2, [67], timing=True)
+    ref = np.load(os.path.join(GOLD, "seam_W2_S67.npz"))["out"]
+    keys = {"norm_mod", "qkv", "a2a_fwd", "fa2_local", "a2a_inv", "out_proj", "residual", "ffn", "gather"}
+    for r in range(2):
+        t = dict(outs[r]["timing_67"])
+        assert set(t) == keys, sorted(t)
+        assert all(float(v) >= 0.0 for v in t.values())
+        assert np.array_equal(outs[r]["seam_67"], ref)
 
 
 @pytest.mark.parametrize("world", [2, 4])
