@@ -74,15 +74,16 @@ int h3_attn_fwd(const void* q, const void* k, const void* v, void* o, int64_t n_
                 float softmax_scale, int32_t* status, void* stream);
 
 /* h3_attn_fwd with an explicit kernel schedule (a tuning hook; h3_attn_fwd uses the
- * default). All variants compute the same attention within the same tolerance; 1, 10 and 11
- * are bit-identical to 0 (same arithmetic in another schedule):
- *   0  two softmax warpgroups run freely, exp2 on MUFU (the default)
- *   1  softmax warpgroups alternate their exp phase (ping-pong token), exp2 on MUFU
- *   2  ping-pong, every 4th element's exp2 on the FMA pipe (degree-3 minimax polynomial)
- *   3  ping-pong, every 8th element on the FMA pipe
- *   4  ping-pong, every 2nd element on the FMA pipe
- *   10 as 0 with one MMA-issuing thread per Q tile; 11 as 10 with the ping-pong token;
- *   12 as 10 with every 8th element's exp2 on the FMA pipe
+ * default). All variants compute the same attention within the same tolerance; variants with
+ * the same exp2 placement are bit-identical to each other (0, 1, 5 | 2, 6):
+ *   0  one CTA per SM, exp2 on MUFU, P handed over after 3 of its 4 32-key chunks (the default)
+ *   1  SM pairs: tcgen05 cta_group::2 MMAs over two CTAs on two SMs, each staging half of every
+ *      K and V tile; otherwise as 0
+ *   2  as 1 with key pairs 2, 6, 10, 14 of 32-key chunks 1-2 on the FMA pipe (a degree-3
+ *      polynomial exp2); 3 the same in chunks 0-2; 4 every other pair of chunks 1-2;
+ *      7 pairs 2, 6, 10 of chunks 0-2; 8 every other pair of chunks 0-2
+ *   5  as 1 with P handed over after 2 of 4 chunks
+ *   6  as 0 with the exp2 placement of 2
  * Returns H3_ERR_UNSUPPORTED for any other value. */
 int h3_attn_fwd_variant(const void* q, const void* k, const void* v, void* o, int64_t n_heads, int64_t s_q,
                         int64_t s_kv, int64_t q_head_stride, int64_t q_row_stride, int64_t kv_head_stride,
@@ -90,13 +91,14 @@ int h3_attn_fwd_variant(const void* q, const void* k, const void* v, void* o, in
                         int64_t o_row_stride, float softmax_scale, int32_t* status, int32_t variant, void* stream);
 
 /* Phase profiler (diagnostics; cf. the clock64 phase counters of the reference kernel,
- * attn_sm80/fa3_sm80_h3.cu:96-105, :572-582): runs variants 0-3, 10 or 11 and records clock64()
+ * attn_sm80/fa3_sm80_h3.cu:96-105, :572-582): runs any variant above and records clock64()
  * stamps of CTA (0, 0) for the first trace_iters KV iterations into the device buffer
  *   trace[((role * trace_iters) + j) * 8 + point]   (int64, 3 * trace_iters * 8 entries)
  * role 0/1 = softmax warpgroup of Q tile 0/1: points 0 before the S wait, 1 S ready,
- *   2 S in registers, 3 row max done, 4 exp phase may start, 5 exps done, 6 P handed over;
- * role 2 = MMA thread: 0 iteration start, 1 P_0 ready, 2 P_0*V issued, 3 next K ready,
- *   4 next S_0 issued, 5 P_1 ready, 6 iteration issued. */
+ *   2 S in registers (second half's load done), 3 row max and any rescale done, 4 first P chunks
+ *   handed over, 5 all of P handed over;
+ * role 2 = MMA thread: 0 iteration start, 1 V ready, 2 first P chunks of tile 0 ready, 3 all of
+ *   P_0 ready, 4 next S_0 issued, 5-7 the same for tile 1. */
 int h3_attn_fwd_profile(const void* q, const void* k, const void* v, void* o, int64_t n_heads, int64_t s_q,
                         int64_t s_kv, int64_t q_head_stride, int64_t q_row_stride, int64_t kv_head_stride,
                         int64_t kv_row_stride, int64_t o_rank_rows, int64_t o_rank_stride, int64_t o_head_stride,

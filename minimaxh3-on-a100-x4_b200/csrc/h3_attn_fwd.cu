@@ -6,7 +6,7 @@
 // attn_sm80/attn_sm80.py:26-31). O = softmax(Q K^T * scale) V per head.
 //
 // CTA = one head x 256 query rows (two 128-row Q tiles), 12 warps:
-//   warp 0      TMA producer: Q tiles once, then K_j / V_j tiles through a 4-stage ring
+//   warp 0      TMA producer: Q tiles once, then K_j / V_j tiles through a 5-stage ring
 //   warp 1      MMA issuer (one thread): S_t = Q_t K_j^T (SS form), O_t += P_t V_j (TS form)
 //   warp 2      TMEM allocator (512 columns)
 //   warps 4-7   softmax warpgroup for Q tile 0; warps 8-11 for Q tile 1
@@ -16,7 +16,7 @@
 // in-register. O is rescaled only when a row max grows by more than 2^8, which
 // keeps P <= 256; every per-row decision depends on that row alone, so a row's
 // result does not depend on which other rows or heads share the launch.
-#include "h3_ptx.cuh"
+#include "h3_pair.cuh"
 #include "h3attn.h"
 
 #include <cmath>
@@ -28,21 +28,27 @@ namespace attn {
 constexpr int kBlockM = 128;
 constexpr int kBlockN = 128;
 constexpr int kRowsPerCta = 2 * kBlockM;
-constexpr int kStages = 5;  // K/V ring: the MMA thread waits for V_j and K_{j+1} a full iteration ahead
+constexpr int kStages = 5;  // K/V ring of whole tiles: the MMA thread waits for V_j and K_{j+1} a full iteration ahead
+constexpr int kMaxRing = 2 * kStages;  // the pair form's ring of half tiles (same bytes)
 constexpr uint32_t kHalfBytes = 128u * 64u * 2u;  // 128 rows x 64 bf16: one 128-B swizzle column block
 constexpr uint32_t kTileBytes = 2u * kHalfBytes;  // 128 rows x 128 bf16
 constexpr int kThreads = 384;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+// Register budgets after the set-up: the producer / MMA / allocator warpgroup needs few, the two
+// softmax warpgroups hold a 128-score row each. 128 * 56 + 256 * 224 = 384 * 168, the launch's total.
+constexpr int kRegsLaunch = 168;
+constexpr int kRegsControl = 56;
+constexpr int kRegsSoftmax = 224;
+static_assert(128 * kRegsControl + 256 * kRegsSoftmax <= kThreads * kRegsLaunch, "register split over budget");
 
 enum Bar : int {
   kBarQFull = 0,
   kBarKVFull = 1,
-  kBarKVEmpty = kBarKVFull + kStages,
-  kBarSFull = kBarKVEmpty + kStages,  // S_t ready (per Q tile)
-  kBarPFullA = kBarSFull + 2,         // first 64 keys of P_t in TMEM
-  kBarPFullB = kBarPFullA + 2,        // last 64 keys of P_t in TMEM
-  kBarODoneA = kBarPFullB + 2,        // P_t,first-half * V retired
-  kBarODone = kBarODoneA + 2,         // P_t * V retired
+  kBarKVEmpty = kBarKVFull + kMaxRing,
+  kBarSFull = kBarKVEmpty + kMaxRing,  // S_t ready (per Q tile)
+  kBarPSplit = kBarSFull + 2,          // P_t chunks [0, kSplit) in TMEM
+  kBarPLast = kBarPSplit + 2,          // all of P_t in TMEM
+  kBarODone = kBarPLast + 2,           // P_t * V retired
   kBarDrain = kBarODone + 2,
   kBarTok = kBarDrain + 1,  // softmax ping-pong token, one per warpgroup
   kNumBars = kBarTok + 2
@@ -112,40 +118,10 @@ __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t a_base, uint3
 #undef H3_QK_STEP
 }
 
-// O (+)= P V over 64 keys (half = 0: keys 0..63, half = 1: keys 64..127) of one tile: P
-// from TMEM (keys along columns, two bf16 per 32-bit column, 8 columns per K step; the
-// second half's P starts p_half_cols columns after the first's), V
-// MN-major in shared memory (d contiguous), two 64-wide d blocks 16 KB apart (LBO), 8-key
-// groups 1 KB apart (SBO); K steps advance 2 KB. `accumulate` applies to the first step.
-__device__ __forceinline__ void issue_pv_half(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_base, int half,
-                                              bool accumulate, uint32_t p_half_cols = 32) {
-  constexpr uint32_t idesc = idesc_bf16_f32(128, 128, 0, 1);
-  const uint64_t bd = smem_desc_sw128(v_base + uint32_t(half) * 4u * 2048u, kHalfBytes, 1024);
-  const uint32_t blo = uint32_t(bd), bhi = uint32_t(bd >> 32);
-  const uint32_t pa = p_tmem + uint32_t(half) * p_half_cols;
-#define H3_PV_STEP(KK) \
-  "add.u32 ta, %1, " #KK "*8;\n\t add.u32 lb, %2, " #KK "*128;\n\t mov.b64 db, {lb, %3};\n\t" \
-  "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], db, %4, pt;\n\t"
-  asm volatile(
-      "{\n\t.reg .pred pf, pt;\n\t.reg .b32 ta, lb;\n\t.reg .b64 db;\n\t"
-      "setp.ne.b32 pf, %5, 0;\n\t setp.eq.b32 pt, %5, %5;\n\t"
-      "mov.b64 db, {%2, %3};\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %4, pf;\n\t"
-      H3_PV_STEP(1) H3_PV_STEP(2) H3_PV_STEP(3)
-      "}\n" ::"r"(d_tmem), "r"(pa), "r"(blo), "r"(bhi), "r"(idesc), "r"(accumulate ? 1u : 0u)
-      : "memory");
-#undef H3_PV_STEP
-}
-
-__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_base, bool accumulate) {
-  issue_pv_half(d_tmem, p_tmem, v_base, 0, accumulate);
-  issue_pv_half(d_tmem, p_tmem, v_base, 1, true);
-}
-
 // Bounded wait that ignores the abort flag: used while draining copies/MMAs before exit.
 __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, int* status) {
   uint64_t t0 = globaltimer_ns();
-  while (!mbar_try_wait(bar, parity)) {
+  while (!mbar_try_wait_sleep(bar, parity)) {
     if (globaltimer_ns() - t0 > H3_WAIT_LIMIT_NS) {
       atomicCAS(status, 0, kStatusTimeoutDrain);
       return;
@@ -153,23 +129,87 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, int* s
   }
 }
 
-// Element idx of a row takes the FMA-pipe exp2 when kEmu > 0 and idx % kEmu == kEmu - 1.
-template <int kEmu>
-__device__ __forceinline__ float ex2_mixed(float x, int idx) {
-  if (kEmu > 0 && (idx % (kEmu > 0 ? kEmu : 1)) == kEmu - 1) return ex2_poly(x);
-  return ex2_approx(x);
+// 2^x of one key pair of 32-key chunk `chunk`, pair `pair` (0..15) in it: on the FMA pipe when
+// bit `pair` of kEmuMask and bit `chunk` of kEmuChunks are set, else on MUFU.
+template <uint32_t kEmuMask, uint32_t kEmuChunks>
+__device__ __forceinline__ void ex2_pair(float x0, float x1, int chunk, int pair, float& y0, float& y1) {
+  if (((kEmuChunks >> chunk) & 1u) && ((kEmuMask >> pair) & 1u)) {
+    ex2_poly2(x0, x1, y0, y1);
+  } else {
+    y0 = ex2_approx(x0);
+    y1 = ex2_approx(x1);
+  }
 }
 
-// kPingPong: the two softmax warpgroups take turns (a token passed through two mbarriers)
-// for their exp phase, so one exponentiates while the tensor core runs the other's
-// P*V and next Q*K^T, instead of both contending for MUFU at once.
-// kDual: one MMA-issuing thread per Q tile (warps 1 and 3) instead of one for both, so a
-// tile's P*V never waits behind the other tile's P hand-off; shared K/V stages are released
-// by both (arrival count 2) and each thread's commits track only its own MMAs.
-template <bool kPingPong, int kEmu, bool kProf, bool kDual = false>
+// O (+)= P V over K steps [kFirst, kFirst + kSteps) of one tile (16 keys per step): P from
+// TMEM at 8 columns per step, V in shared memory 2 KB per step. One asm block per call.
+template <int kFirst, int kSteps>
+__device__ __forceinline__ void issue_pv_steps(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_base, bool accumulate) {
+  static_assert(kFirst >= 0 && kSteps >= 0 && kFirst + kSteps <= 8, "8 K steps per tile");
+  if constexpr (kSteps > 0) {
+    constexpr uint32_t idesc = idesc_bf16_f32(128, 128, 0, 1);
+    // steps 0-3 sit in the first 64-key block of V's rows, 4-7 in the second (8 KB on); the two
+    // 64-wide d blocks are 16 KB apart (LBO), 8-key groups 1 KB apart (SBO)
+    const uint64_t bd = smem_desc_sw128(v_base + uint32_t(kFirst) * 2048u, kHalfBytes, 1024);
+    const uint32_t blo = uint32_t(bd), bhi = uint32_t(bd >> 32);
+    const uint32_t pa = p_tmem + uint32_t(kFirst) * 8u;
+#define H3_PV_STEP(KK) \
+  "add.u32 ta, %1, " #KK "*8;\n\t add.u32 lb, %2, " #KK "*128;\n\t mov.b64 db, {lb, %3};\n\t" \
+  "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], db, %4, pt;\n\t"
+#define H3_PV_HEAD \
+  "{\n\t.reg .pred pf, pt;\n\t.reg .b32 ta, lb;\n\t.reg .b64 db;\n\t" \
+  "setp.ne.b32 pf, %5, 0;\n\t setp.eq.b32 pt, %5, %5;\n\t mov.b64 db, {%2, %3};\n\t" \
+  "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %4, pf;\n\t"
+#define H3_PV_ARGS ::"r"(d_tmem), "r"(pa), "r"(blo), "r"(bhi), "r"(idesc), "r"(accumulate ? 1u : 0u) : "memory"
+    if constexpr (kSteps == 1) {
+      asm volatile(H3_PV_HEAD "}\n" H3_PV_ARGS);
+    } else if constexpr (kSteps == 2) {
+      asm volatile(H3_PV_HEAD H3_PV_STEP(1) "}\n" H3_PV_ARGS);
+    } else if constexpr (kSteps == 4) {
+      asm volatile(H3_PV_HEAD H3_PV_STEP(1) H3_PV_STEP(2) H3_PV_STEP(3) "}\n" H3_PV_ARGS);
+    } else if constexpr (kSteps == 6) {
+      asm volatile(H3_PV_HEAD H3_PV_STEP(1) H3_PV_STEP(2) H3_PV_STEP(3) H3_PV_STEP(4) H3_PV_STEP(5) "}\n" H3_PV_ARGS);
+    } else if constexpr (kSteps == 8) {
+      asm volatile(H3_PV_HEAD H3_PV_STEP(1) H3_PV_STEP(2) H3_PV_STEP(3) H3_PV_STEP(4) H3_PV_STEP(5) H3_PV_STEP(6)
+                       H3_PV_STEP(7) "}\n" H3_PV_ARGS);
+    } else {
+      static_assert(kSteps == 1 || kSteps == 2 || kSteps == 4 || kSteps == 6 || kSteps == 8, "step count");
+    }
+#undef H3_PV_ARGS
+#undef H3_PV_HEAD
+#undef H3_PV_STEP
+  }
+}
+
+// One warp-specialised CTA (see the header). Per KV tile j and Q tile t:
+//   MMA thread   waits P_t(j) chunks 0..kSplit-1 -> P_t V_j over their K steps; waits the
+//                rest -> the remaining K steps -> S_t = Q_t K_{j+1}^T (overwrites P_t).
+//   softmax t    waits S_t(j), loads its 128 scores, takes the row max over all 128 keys
+//                (three-input max), rescales O_t when the max grew by more than 2^8, then
+//                exponentiates in four 32-key chunks, storing each chunk's bf16 P into TMEM
+//                and handing chunks [0, kSplit) over before computing the rest.
+// So after the last exponential only (4 - kSplit) chunks of P V and one Q K^T stand between
+// a tile's softmax and its next S. O_t is quiescent when S_t(j) is ready: the MMA thread
+// issued every P_t V of iteration j-1 before S_t(j) = Q_t K_j^T, and its commit retires
+// everything issued earlier.
+// kPair: the CTA is one of a two-CTA cluster on two SMs whose tile t rows form one M = 256
+// pair MMA (tcgen05 cta_group::2) issued by the even CTA's MMA thread: each SM stages half
+// of every K tile (64 keys) and of every V tile (64 head-dimension columns) through a 10-stage
+// ring of 16 KB halves, so a Q K^T MMA reads 6 KB of shared memory per SM instead of 8 KB and
+// the per-SM K/V traffic halves. Commits reach both CTAs' barriers; the softmax warps of both
+// CTAs hand P over on the even CTA's barriers (one arrival per warp).
+// kEmuMask / kEmuChunks: which key pairs take the FMA-pipe exp2 (pair positions inside a
+// 32-key chunk / chunks; zero: all on MUFU).
+// kPingPong: the two softmax warpgroups take turns for their exponentials (a token passed
+// through two mbarriers).
+template <bool kPair, uint32_t kEmuMask, uint32_t kEmuChunks, int kSplit, bool kPingPong, bool kProf>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                     const __grid_constant__ CUtensorMap tmap_v, const Params p) {
+  static_assert(kSplit >= 1 && kSplit <= 4, "P hand-off after 1..4 of the 4 chunks");
+  constexpr int kRing = kPair ? 2 * kStages : kStages;             // ring stages
+  constexpr uint32_t kStage = kPair ? kTileBytes / 2 : kTileBytes;  // bytes per stage
+  constexpr uint32_t kPCount = kPair ? 8 : 128;                     // P hand-off arrivals
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
@@ -180,25 +220,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = kPair ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
   const int head = blockIdx.y;
-  const int m0 = blockIdx.x * kRowsPerCta;
+  // this CTA's rows: tile t covers [m0 + 128 t, m0 + 128 t + 128); a pair covers 512 rows
+  const int m0 = kPair ? (blockIdx.x >> 1) * (2 * kRowsPerCta) + kRowsPerCta * int(rank) : blockIdx.x * kRowsPerCta;
   const int n_kv = p.n_kv_tiles;
 
   if (threadIdx.x == 0) {
     mbar_init(bar(kBarQFull), 1);
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kRing; ++s) {
       mbar_init(bar(kBarKVFull + s), 1);
-      mbar_init(bar(kBarKVEmpty + s), kDual ? 2 : 1);
+      mbar_init(bar(kBarKVEmpty + s), 1);
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(bar(kBarSFull + t), 1);
-      mbar_init(bar(kBarPFullA + t), 128);
-      mbar_init(bar(kBarPFullB + t), 128);
-      mbar_init(bar(kBarODoneA + t), 1);
+      mbar_init(bar(kBarPSplit + t), kPCount);
+      mbar_init(bar(kBarPLast + t), kPCount);
       mbar_init(bar(kBarODone + t), 1);
       mbar_init(bar(kBarTok + t), 128);
     }
-    mbar_init(bar(kBarDrain), kDual ? 2 : 1);
+    mbar_init(bar(kBarDrain), 1);
     *abort_flag = (*reinterpret_cast<volatile int*>(p.status) != 0) ? 1 : 0;
     fence_mbar_init();
   }
@@ -208,160 +250,175 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmap_v);
   }
   if (warp == 2) {
-    tmem_alloc(smem_u32(tmem_slot), 512);
-    tmem_relinquish();
+    if constexpr (kPair) {
+      tmem_alloc_pair(smem_u32(tmem_slot), 512);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(smem_u32(tmem_slot), 512);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (kPair)
+    cluster_sync_all();  // barriers and TMEM of both CTAs exist before anything remote touches them
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const WaitCtx ctx{abort_flag, p.status};
   const bool grid_aborted = *abort_flag != 0;
-
-  if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
-    if (lane == 0 && !grid_aborted) {
-      const uint32_t sq = sbase + kOffQ;
-      const uint32_t skv = sbase + kOffKV;
-      mbar_expect_tx(bar(kBarQFull), 2 * kTileBytes);
-      for (int t = 0; t < 2; ++t)
-        for (int hh = 0; hh < 2; ++hh)
-          tma_load_3d(sq + t * kTileBytes + hh * kHalfBytes, &tmap_q, bar(kBarQFull), hh * 64, m0 + t * kBlockM,
-                      head);
-      int it = 0;
-      for (int j = 0; j < n_kv; ++j) {
-        bool ok = true;
-        for (int kv = 0; kv < 2; ++kv, ++it) {
-          const int st = it % kStages;
-          const uint32_t ph = uint32_t(it / kStages) & 1u;
-          if (!mbar_wait(bar(kBarKVEmpty + st), ph ^ 1u, ctx, kStatusTimeoutKV)) {
-            ok = false;
-            break;
+  if (warp < 4) {
+    regs_dec<kRegsControl>();
+    if (warp == 0) {
+      // ------------------------------------------------------------ TMA producer
+      // Ring order K_0, V_0, K_1, V_1, ...; in the pair form each CTA loads its halves and the
+      // copies of both CTAs count on the even CTA's full barriers.
+      if (lane == 0 && !grid_aborted) {
+        const uint32_t sq = sbase + kOffQ;
+        const uint32_t skv = sbase + kOffKV;
+        const uint32_t q_full = kPair ? mapa_shared(bar(kBarQFull), 0) : bar(kBarQFull);
+        if (leader) mbar_expect_tx(bar(kBarQFull), (kPair ? 4 : 2) * kTileBytes);
+        for (int t = 0; t < 2; ++t)
+          for (int hh = 0; hh < 2; ++hh) {
+            if constexpr (kPair)
+              tma_load_3d_pair(sq + t * kTileBytes + hh * kHalfBytes, &tmap_q, q_full, hh * 64, m0 + t * kBlockM,
+                               head);
+            else
+              tma_load_3d(sq + t * kTileBytes + hh * kHalfBytes, &tmap_q, q_full, hh * 64, m0 + t * kBlockM, head);
           }
-          const CUtensorMap* m = kv ? &tmap_v : &tmap_k;
-          mbar_expect_tx(bar(kBarKVFull + st), kTileBytes);
-          tma_load_3d(skv + st * kTileBytes, m, bar(kBarKVFull + st), 0, j * kBlockN, head);
-          tma_load_3d(skv + st * kTileBytes + kHalfBytes, m, bar(kBarKVFull + st), 64, j * kBlockN, head);
-        }
-        if (!ok) break;
-      }
-      // Every issued copy must land before the CTA may exit.
-      drain_wait(bar(kBarQFull), 0, p.status);
-      for (int st = 0; st < kStages; ++st) {
-        const int cnt = it / kStages + (st < it % kStages ? 1 : 0);
-        if (cnt > 0) drain_wait(bar(kBarKVFull + st), uint32_t(cnt - 1) & 1u, p.status);
-      }
-    }
-  } else if (kDual && (warp == 1 || warp == 3)) {
-    // ------------------------------------------------------------ MMA issuer for one Q tile
-    if (lane == 0 && !grid_aborted) {
-      const int t = warp == 1 ? 0 : 1;
-      const uint32_t sq = sbase + kOffQ + t * kTileBytes;
-      const uint32_t skv = sbase + kOffKV;
-      const bool rec = t == 0 && blockIdx.x == 0 && blockIdx.y == 0;
-      auto wait_full = [&](int st_it) -> bool {
-        return mbar_wait(bar(kBarKVFull + st_it % kStages), uint32_t(st_it / kStages) & 1u, ctx, kStatusTimeoutKV);
-      };
-      // smem operands arrive by TMA: the mbarrier wait orders them; the tcgen05 fence is only
-      // needed after waits on P, which other threads wrote with tcgen05.st.
-      bool ok = mbar_wait(bar(kBarQFull), 0, ctx, kStatusTimeoutQ) && wait_full(0);
-      if (ok) {
-        issue_qk(tmem + col_s(t), sq, skv);
-        mma_commit(bar(kBarSFull + t));
-        mma_commit(bar(kBarKVEmpty + 0));
-      }
-      for (int j = 0; ok && j < n_kv; ++j) {
-        prof_mark<kProf>(p, rec, 2, j, 0);
-        const int it_v = 2 * j + 1, it_k = 2 * j + 2;
-        const uint32_t ph = uint32_t(j) & 1u;
-        if (!(ok = wait_full(it_v))) break;
-        const uint32_t sv = skv + (it_v % kStages) * kTileBytes;
-        prof_mark<kProf>(p, rec, 2, j, 1);
-        if (!(ok = mbar_wait(bar(kBarPFullA + t), ph, ctx, kStatusTimeoutP))) break;
-        prof_mark<kProf>(p, rec, 2, j, 2);
-        tc_fence_after();
-        issue_pv_half(tmem + col_o(t), tmem + col_p(t), sv, 0, j > 0);
-        mma_commit(bar(kBarODoneA + t));
-        if (!(ok = mbar_wait(bar(kBarPFullB + t), ph, ctx, kStatusTimeoutP))) break;
-        prof_mark<kProf>(p, rec, 2, j, 3);
-        tc_fence_after();
-        issue_pv_half(tmem + col_o(t), tmem + col_p(t), sv, 1, true);
-        mma_commit(bar(kBarODone + t));
-        mma_commit(bar(kBarKVEmpty + it_v % kStages));
-        if (j + 1 < n_kv) {
-          if (!(ok = wait_full(it_k))) break;
-          prof_mark<kProf>(p, rec, 2, j, 4);
-          issue_qk(tmem + col_s(t), sq, skv + (it_k % kStages) * kTileBytes);
-          mma_commit(bar(kBarSFull + t));
-          mma_commit(bar(kBarKVEmpty + it_k % kStages));
-        }
-        prof_mark<kProf>(p, rec, 2, j, 5);
-      }
-      mma_commit(bar(kBarDrain));
-      drain_wait(bar(kBarDrain), 0, p.status);
-    }
-  } else if (!kDual && warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    // Ring order is K_0, V_0, K_1, V_1, ...; iteration j holds V_j and K_{j+1}. Both are
-    // waited for before any P of iteration j, so no barrier wait sits between P_t * V_j
-    // and the next S_t = Q_t K_{j+1}^T.
-    if (lane == 0 && !grid_aborted) {
-      const uint32_t sq = sbase + kOffQ;
-      const uint32_t skv = sbase + kOffKV;
-      const bool rec = blockIdx.x == 0 && blockIdx.y == 0;
-      auto wait_full = [&](int st_it) -> bool {
-        return mbar_wait(bar(kBarKVFull + st_it % kStages), uint32_t(st_it / kStages) & 1u, ctx, kStatusTimeoutKV);
-      };
-      bool ok = mbar_wait(bar(kBarQFull), 0, ctx, kStatusTimeoutQ) && wait_full(0);
-      if (ok) {
-        tc_fence_after();
-        issue_qk(tmem + col_s(0), sq, skv);
-        mma_commit(bar(kBarSFull + 0));
-        issue_qk(tmem + col_s(1), sq + kTileBytes, skv);
-        mma_commit(bar(kBarSFull + 1));
-        mma_commit(bar(kBarKVEmpty + 0));
-      }
-      for (int j = 0; ok && j < n_kv; ++j) {
-        prof_mark<kProf>(p, rec, 2, j, 0);
-        const int it_v = 2 * j + 1, it_k = 2 * j + 2;
-        const bool next = j + 1 < n_kv;
-        // smem operands arrive by TMA, ordered by the mbarrier wait alone; a tcgen05 fence is
-        // needed only after the waits on P, which other threads wrote with tcgen05.st.
-        if (!(ok = wait_full(it_v))) break;
-        const uint32_t sv = skv + (it_v % kStages) * kTileBytes;
-        const uint32_t sk = skv + (it_k % kStages) * kTileBytes;
-        const uint32_t ph = uint32_t(j) & 1u;
-        prof_mark<kProf>(p, rec, 2, j, 1);
-        for (int t = 0; t < 2; ++t) {
-          if (!(ok = mbar_wait(bar(kBarPFullA + t), ph, ctx, kStatusTimeoutP))) break;
-          prof_mark<kProf>(p, rec, 2, j, 2 + 3 * t);
-          tc_fence_after();
-          issue_pv_half(tmem + col_o(t), tmem + col_p(t), sv, 0, j > 0);
-          mma_commit(bar(kBarODoneA + t));
-          if (!(ok = mbar_wait(bar(kBarPFullB + t), ph, ctx, kStatusTimeoutP))) break;
-          prof_mark<kProf>(p, rec, 2, j, 3 + 3 * t);
-          tc_fence_after();
-          issue_pv_half(tmem + col_o(t), tmem + col_p(t), sv, 1, true);
-          mma_commit(bar(kBarODone + t));
-          if (t == 1) mma_commit(bar(kBarKVEmpty + it_v % kStages));
-          if (next) {
-            if (t == 0 && !(ok = wait_full(it_k))) break;  // overlaps the queued P*V work
-            issue_qk(tmem + col_s(t), sq + t * kTileBytes, sk);
-            mma_commit(bar(kBarSFull + t));
-            if (t == 1) mma_commit(bar(kBarKVEmpty + it_k % kStages));
+        int it = 0;
+        for (int j = 0; j < n_kv; ++j) {
+          bool ok = true;
+          for (int kv = 0; kv < 2; ++kv, ++it) {
+            const int st = it % kRing;
+            const uint32_t ph = uint32_t(it / kRing) & 1u;
+            if (!mbar_wait(bar(kBarKVEmpty + st), ph ^ 1u, ctx, kStatusTimeoutKV)) {
+              ok = false;
+              break;
+            }
+            const uint32_t dst = skv + st * kStage;
+            if constexpr (kPair) {
+              const uint32_t full = mapa_shared(bar(kBarKVFull + st), 0);
+              if (leader) mbar_expect_tx(bar(kBarKVFull + st), kTileBytes);
+              if (kv == 0) {  // K: this CTA's 64 keys, both 64-column blocks (64-row boxes)
+                for (int hh = 0; hh < 2; ++hh)
+                  tma_load_3d_pair(dst + hh * (kStage / 2), &tmap_k, full, hh * 64, j * kBlockN + 64 * int(rank),
+                                   head);
+              } else {  // V: all 128 keys, this CTA's 64 head-dimension columns
+                tma_load_3d_pair(dst, &tmap_v, full, 64 * int(rank), j * kBlockN, head);
+              }
+            } else {
+              const CUtensorMap* m = kv ? &tmap_v : &tmap_k;
+              mbar_expect_tx(bar(kBarKVFull + st), kTileBytes);
+              tma_load_3d(dst, m, bar(kBarKVFull + st), 0, j * kBlockN, head);
+              tma_load_3d(dst + kHalfBytes, m, bar(kBarKVFull + st), 64, j * kBlockN, head);
+            }
           }
-          prof_mark<kProf>(p, rec, 2, j, 4 + 3 * t);
+          if (!ok) break;
+        }
+        // Every issued copy must land before the CTA may exit (the pair's copies all count on the
+        // even CTA's barriers; the odd CTA cannot leave before the final cluster barrier).
+        if (leader) {
+          auto drain = [&](uint32_t b, uint32_t par) {
+            if constexpr (kPair)
+              pair::drain_wait_pair(b, par, p.status);
+            else
+              drain_wait(b, par, p.status);
+          };
+          drain(bar(kBarQFull), 0);
+          for (int st = 0; st < kRing; ++st) {
+            const int cnt = it / kRing + (st < it % kRing ? 1 : 0);
+            if (cnt > 0) drain(bar(kBarKVFull + st), uint32_t(cnt - 1) & 1u);
+          }
         }
       }
-      // Every issued MMA must retire before TMEM is released.
-      mma_commit(bar(kBarDrain));
-      drain_wait(bar(kBarDrain), 0, p.status);
+    } else if (warp == 1) {
+      // ------------------------------------------------------------ MMA issuer (even CTA)
+      if (lane == 0 && leader && !grid_aborted) {
+        const uint32_t sq = sbase + kOffQ;
+        const uint32_t skv = sbase + kOffKV;
+        const bool rec = blockIdx.x == 0 && blockIdx.y == 0;
+        // waits on barriers that the other CTA's threads or copies complete take cluster scope
+        auto wait_x = [&](uint32_t b, uint32_t par, int code) -> bool {
+          if constexpr (kPair)
+            return mbar_wait_cluster(b, par, ctx, code);
+          else
+            return mbar_wait(b, par, ctx, code);
+        };
+        auto wait_full = [&](int st_it) -> bool {
+          return wait_x(bar(kBarKVFull + st_it % kRing), uint32_t(st_it / kRing) & 1u, kStatusTimeoutKV);
+        };
+        auto commit = [&](int b) {
+          if constexpr (kPair)
+            mma_commit_pair(bar(b), 0x3);
+          else
+            mma_commit(bar(b));
+        };
+        auto qk = [&](int t, uint32_t k_base) {
+          if constexpr (kPair)
+            pair::issue_qk_pair(tmem + col_s(t), sq + t * kTileBytes, k_base);
+          else
+            issue_qk(tmem + col_s(t), sq + t * kTileBytes, k_base);
+        };
+        bool ok = wait_x(bar(kBarQFull), 0, kStatusTimeoutQ) && wait_full(0);
+        if (ok) {
+          tc_fence_after();
+          qk(0, skv);
+          commit(kBarSFull + 0);
+          qk(1, skv);
+          commit(kBarSFull + 1);
+          commit(kBarKVEmpty + 0);
+        }
+        for (int j = 0; ok && j < n_kv; ++j) {
+          prof_mark<kProf>(p, rec, 2, j, 0);
+          const int it_v = 2 * j + 1, it_k = 2 * j + 2;
+          const bool next = j + 1 < n_kv;
+          // smem operands arrive by TMA, ordered by the mbarrier wait alone; a tcgen05 fence is
+          // needed only after the waits on P, which other threads wrote with tcgen05.st.
+          if (!(ok = wait_full(it_v))) break;
+          const uint32_t sv = skv + (it_v % kRing) * kStage;
+          const uint32_t sk = skv + (it_k % kRing) * kStage;
+          const uint32_t ph = uint32_t(j) & 1u;
+          prof_mark<kProf>(p, rec, 2, j, 1);
+          for (int t = 0; t < 2; ++t) {
+            if (!(ok = wait_x(bar(kBarPSplit + t), ph, kStatusTimeoutP))) break;
+            prof_mark<kProf>(p, rec, 2, j, 2 + 3 * t);
+            tc_fence_after();
+            if constexpr (kPair)
+              pair::issue_pv_pair_steps<0, 2 * kSplit>(tmem + col_o(t), tmem + col_p(t), sv, j > 0);
+            else
+              issue_pv_steps<0, 2 * kSplit>(tmem + col_o(t), tmem + col_p(t), sv, j > 0);
+            if (!(ok = wait_x(bar(kBarPLast + t), ph, kStatusTimeoutP))) break;
+            prof_mark<kProf>(p, rec, 2, j, 3 + 3 * t);
+            tc_fence_after();
+            if constexpr (kPair)
+              pair::issue_pv_pair_steps<2 * kSplit, 8 - 2 * kSplit>(tmem + col_o(t), tmem + col_p(t), sv, true);
+            else
+              issue_pv_steps<2 * kSplit, 8 - 2 * kSplit>(tmem + col_o(t), tmem + col_p(t), sv, true);
+            commit(kBarODone + t);
+            if (t == 1) commit(kBarKVEmpty + it_v % kRing);
+            if (next) {
+              if (t == 0 && !(ok = wait_full(it_k))) break;  // overlaps the queued P*V work
+              qk(t, sk);
+              commit(kBarSFull + t);
+              if (t == 1) commit(kBarKVEmpty + it_k % kRing);
+            }
+            prof_mark<kProf>(p, rec, 2, j, 4 + 3 * t);
+          }
+        }
+        // Every issued MMA must retire before TMEM is released.
+        if constexpr (kPair) {
+          mma_commit_pair(bar(kBarDrain), 0x1);
+          pair::drain_wait_pair(bar(kBarDrain), 0, p.status);
+        } else {
+          mma_commit(bar(kBarDrain));
+          drain_wait(bar(kBarDrain), 0, p.status);
+        }
+      }
     }
-  } else if (warp >= 4) {
+  } else {
+    regs_inc<kRegsSoftmax>();
     // ------------------------------------------------------------ softmax + epilogue
-    // The 128 keys of a tile are handled as two 64-key halves: each half has its own row
-    // max / rescale step and its own P hand-off, so P_a * V runs on the tensor core while
-    // the second half's exponentials are computed. Online softmax across halves is exact.
     const int t = (warp - 4) >> 2;  // Q tile
     const int quad = warp & 3;      // TMEM lane quadrant this warp may access
     const uint32_t lane_off = uint32_t(quad * 32) << 16;
@@ -369,34 +426,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tP = tmem + lane_off + col_p(t);
     const uint32_t tO = tmem + lane_off + col_o(t);
     const float c = p.scale_log2;
+    const uint64_t c2 = f2_pack(c, c);
     const int tail_valid = p.s_kv - (n_kv - 1) * kBlockN;
     float m_run = -INFINITY;
-    float l_run = 0.f;
+    uint64_t l_a = f2_pack(0.f, 0.f), l_b = f2_pack(0.f, 0.f);  // packed partial row sums
     bool ok = !grid_aborted;
     const bool rec = blockIdx.x == 0 && blockIdx.y == 0 && quad == 0 && lane == 0;
-
-    // Rescale O (and l) of the rows whose running max grew by more than 2^8; `o_ready`
-    // says whether every P*V accumulated so far has retired.
-    auto rescale = [&](float m_new, uint32_t o_bar, uint32_t o_parity, bool o_ready) -> bool {
-      const bool need = m_new > m_run + kRescaleThreshold;
-      if (!__any_sync(0xffffffffu, need)) return true;
-      if (!o_ready && !__all_sync(0xffffffffu, mbar_wait(o_bar, o_parity, ctx, kStatusTimeoutO))) return false;
-      tc_fence_after();
-      const float f = need ? ex2_approx(m_run - m_new) : 1.0f;
-      if (need) {
-        l_run *= f;
-        m_run = m_new;
-      }
-#pragma unroll 1
-      for (int c16 = 0; c16 < 8; ++c16) {
-        uint32_t o[16];
-        tmem_ld16_wait(tO + c16 * 16, o);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
-        tmem_st16(tO + c16 * 16, o);
-      }
+    // P hand-off: every thread's stores are complete and fenced; then one arrival per thread on
+    // this CTA's barrier, or (pair form) one per warp on the even CTA's barrier
+    auto hand_over = [&](int b) {
       tmem_st_wait();
-      return true;
+      tc_fence_before();
+      if constexpr (kPair) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(mapa_shared(bar(b), 0));
+      } else {
+        mbar_arrive(bar(b));
+      }
     };
 
     for (int j = 0; ok && j < n_kv; ++j) {
@@ -405,79 +451,116 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       prof_mark<kProf>(p, rec, t, j, 1);
       tc_fence_after();
+      // S in two 64-column halves: the second half's load is in flight while the first half's
+      // maximum is taken
       uint32_t sa[64], sb[64];
       tmem_ld64_wait(tS, sa);
-      tmem_ld64_wait(tS + 64, sb);
+      tmem_ld64_nowait(tS + 64, sb);
       float s[128];
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        s[i] = __uint_as_float(sa[i]);
-        s[64 + i] = __uint_as_float(sb[i]);
-      }
-      if (j == n_kv - 1 && tail_valid < kBlockN) {
+      for (int i = 0; i < 64; ++i) s[i] = __uint_as_float(sa[i]);
+      const bool tail = j == n_kv - 1 && tail_valid < kBlockN;
+      if (tail) {
 #pragma unroll
-        for (int i = 0; i < 128; ++i)
+        for (int i = 0; i < 64; ++i)
+          if (i >= tail_valid) s[i] = -INFINITY;
+      }
+      // row max over the tile's 128 keys: four chains of three-input maxima
+      float mx0 = fmax3(s[0], s[1], s[2]), mx1 = fmax3(s[3], s[4], s[5]);
+      float mx2 = fmax3(s[6], s[7], s[8]), mx3 = fmax3(s[9], s[10], s[11]);
+#pragma unroll
+      for (int i = 12; i < 60; i += 8) {
+        mx0 = fmax3(mx0, s[i], s[i + 1]);
+        mx1 = fmax3(mx1, s[i + 2], s[i + 3]);
+        mx2 = fmax3(mx2, s[i + 4], s[i + 5]);
+        mx3 = fmax3(mx3, s[i + 6], s[i + 7]);
+      }
+      mx0 = fmax3(mx0, s[60], s[61]);
+      mx1 = fmax3(mx1, s[62], s[63]);
+      tmem_ld64_wait_on(sb);
+#pragma unroll
+      for (int i = 0; i < 64; ++i) s[64 + i] = __uint_as_float(sb[i]);
+      if (tail) {
+#pragma unroll
+        for (int i = 64; i < 128; ++i)
           if (i >= tail_valid) s[i] = -INFINITY;
       }
       prof_mark<kProf>(p, rec, t, j, 2);
+#pragma unroll
+      for (int i = 64; i < 120; i += 8) {
+        mx0 = fmax3(mx0, s[i], s[i + 1]);
+        mx1 = fmax3(mx1, s[i + 2], s[i + 3]);
+        mx2 = fmax3(mx2, s[i + 4], s[i + 5]);
+        mx3 = fmax3(mx3, s[i + 6], s[i + 7]);
+      }
+      mx0 = fmax3(mx0, s[120], s[121]);
+      mx1 = fmax3(mx1, s[122], s[123]);
+      mx2 = fmax3(mx2, s[124], s[125]);
+      mx3 = fmax3(mx3, s[126], s[127]);
+      const float m_new = fmaxf(m_run, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * c);
+      if (j == 0) {
+        m_run = m_new;
+      } else {
+        // Rescale O (and l) of the rows whose running max grew by more than 2^8. O_t is
+        // quiescent here (S_t(j) ready implies every earlier P_t V has retired).
+        const bool need = m_new > m_run + kRescaleThreshold;
+        if (__any_sync(0xffffffffu, need)) {
+          const float f = need ? ex2_approx(m_run - m_new) : 1.0f;
+          if (need) {
+            l_a = f2_fma(l_a, f2_pack(f, f), f2_pack(0.f, 0.f));
+            l_b = f2_fma(l_b, f2_pack(f, f), f2_pack(0.f, 0.f));
+            m_run = m_new;
+          }
+#pragma unroll 1
+          for (int c16 = 0; c16 < 8; ++c16) {
+            uint32_t o[16];
+            tmem_ld16_wait(tO + c16 * 16, o);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+            tmem_st16(tO + c16 * 16, o);
+          }
+          tmem_st_wait();
+        }
+      }
+      prof_mark<kProf>(p, rec, t, j, 3);
       if (kPingPong && (t == 1 || j > 0)) {
         const uint32_t par = t == 0 ? uint32_t(j - 1) & 1u : uint32_t(j) & 1u;
         ok = __all_sync(0xffffffffu, mbar_wait(bar(kBarTok + t), par, ctx, kStatusTimeoutS));
         if (!ok) break;
       }
+      // exponentials in four 32-key chunks, each stored as bf16 P as soon as it is done; the
+      // fp32 values stay in s[] for the row sum, which is taken after P has been handed over
+      const uint64_t nm2 = f2_pack(-m_run, -m_run);
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        float l0, l1, l2, l3;
-        uint32_t pk[32];
-        // h = 0: S_t(j) ready implies every earlier P*V of this tile has retired; h = 1: O holds
-        // the first half of P_t(j) once o_done_a (phase j) completes
-        auto do_rescale = [&](float m_new) -> bool {
-          return h == 0 ? rescale(m_new, 0, 0, true) : rescale(m_new, bar(kBarODoneA + t), uint32_t(j) & 1u, false);
-        };
-        // every half holds at least one live key except possibly the second half of the last tile
-        float mx0 = s[64 * h], mx1 = s[64 * h + 1], mx2 = s[64 * h + 2], mx3 = s[64 * h + 3];
+      for (int k = 0; k < 4; ++k) {
+        uint32_t pk[16];
 #pragma unroll
-        for (int i = 4; i < 64; i += 4) {
-          mx0 = fmaxf(mx0, s[64 * h + i]);
-          mx1 = fmaxf(mx1, s[64 * h + i + 1]);
-          mx2 = fmaxf(mx2, s[64 * h + i + 2]);
-          mx3 = fmaxf(mx3, s[64 * h + i + 3]);
+        for (int i = 0; i < 16; ++i) {
+          const int e = 32 * k + 2 * i;
+          float x0, x1;
+          f2_unpack(f2_fma(f2_pack(s[e], s[e + 1]), c2, nm2), x0, x1);
+          ex2_pair<kEmuMask, kEmuChunks>(x0, x1, k, i, s[e], s[e + 1]);
+          pk[i] = pack_bf16x2(s[e], s[e + 1]);
         }
-        const float m_new = fmaxf(m_run, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * c);
-        if (j == 0 && h == 0) {
-          m_run = m_new;
-        } else if (!(ok = do_rescale(m_new))) {
-          break;
+        tmem_st16(tP + 16 * k, pk);
+        if (k == kSplit - 1) {
+          hand_over(kBarPSplit + t);
+          prof_mark<kProf>(p, rec, t, j, 4);
         }
-        prof_mark<kProf>(p, rec, t, j, 3 + 2 * h);
-        // exponentials of this half against m_run
-        {
-          const float neg_m = -m_run;
-          l0 = l1 = l2 = l3 = 0.f;
+      }
+      if (kPingPong) mbar_arrive(bar(kBarTok + (t ^ 1)));  // hand the exp phase over
+      hand_over(kBarPLast + t);
+      prof_mark<kProf>(p, rec, t, j, 5);
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const int e = 64 * h + 2 * i;
-            const float e0 = ex2_mixed<kEmu>(fmaf(s[e], c, neg_m), e);
-            const float e1 = ex2_mixed<kEmu>(fmaf(s[e + 1], c, neg_m), e + 1);
-            const float e2 = ex2_mixed<kEmu>(fmaf(s[e + 2], c, neg_m), e + 2);
-            const float e3 = ex2_mixed<kEmu>(fmaf(s[e + 3], c, neg_m), e + 3);
-            l0 += e0;
-            l1 += e1;
-            l2 += e2;
-            l3 += e3;
-            pk[i] = pack_bf16x2(e0, e1);
-            pk[i + 1] = pack_bf16x2(e2, e3);
-          }
-        }
-        if (kPingPong && h == 1) mbar_arrive(bar(kBarTok + (t ^ 1)));  // hand the exp phase over
-        l_run += (l0 + l1) + (l2 + l3);
-        tmem_st32(tP + 32 * h, pk);
-        tmem_st_wait();
-        tc_fence_before();
-        mbar_arrive(bar(h == 0 ? kBarPFullA + t : kBarPFullB + t));
-        prof_mark<kProf>(p, rec, t, j, 4 + 2 * h);
+      for (int i = 0; i < 128; i += 4) {
+        l_a = f2_add(l_a, f2_pack(s[i], s[i + 1]));
+        l_b = f2_add(l_b, f2_pack(s[i + 2], s[i + 3]));
       }
     }
+    float la0, la1, lb0, lb1;
+    f2_unpack(l_a, la0, la1);
+    f2_unpack(l_b, lb0, lb1);
+    const float l_run = (la0 + la1) + (lb0 + lb1);
     if (ok) {
       ok = __all_sync(0xffffffffu,
                       mbar_wait(bar(kBarODone + t), uint32_t(n_kv - 1) & 1u, ctx, kStatusTimeoutO));
@@ -542,9 +625,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (kPair) cluster_sync_all();  // the pair MMAs into this CTA's TMEM have retired
   if (warp == 2) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    if constexpr (kPair)
+      tmem_dealloc_pair(tmem, 512);
+    else
+      tmem_dealloc(tmem, 512);
   }
 }
 
@@ -656,7 +743,7 @@ __global__ void __launch_bounds__(128, 1)
     for (int hh = 0; hh < 2; ++hh) tma_load_3d(sbase + hh * kHalfBytes, &tmap_v, b_full, hh * 64, 0, 0);
     if (mbar_wait(b_full, 0, ctx, kStatusTimeoutKat)) {
       tc_fence_after();
-      issue_pv(tmem + 128, tmem + 64, sbase, false);
+      issue_pv_steps<0, 8>(tmem + 128, tmem + 64, sbase, false);
     } else {
       drain_wait(b_full, 0, status);
     }
@@ -744,14 +831,14 @@ static EncodeTiledFn get_encode_fn() {
   return reinterpret_cast<EncodeTiledFn>(fn);
 }
 
-// [n_heads][rows][128] bf16 with element strides (row_stride, head_stride); box 64 x 128 x 1, SW128.
+// [n_heads][rows][128] bf16 with element strides (row_stride, head_stride); box 64 x box_rows x 1, SW128.
 static int make_head_map(CUtensorMap* map, const void* base, long long rows, long long n_heads,
-                         long long row_stride, long long head_stride) {
+                         long long row_stride, long long head_stride, unsigned box_rows = 128) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return H3_ERR_DRIVER;
   cuuint64_t dims[3] = {128, (cuuint64_t)rows, (cuuint64_t)n_heads};
   cuuint64_t strides[2] = {(cuuint64_t)row_stride * 2, (cuuint64_t)head_stride * 2};
-  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t box[3] = {64, box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -766,14 +853,53 @@ static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 using namespace h3::attn;
 
-template <bool kPingPong, int kEmu, bool kProf = false, bool kDual = false>
-static int launch_variant(dim3 grid, cudaStream_t st, const CUtensorMap& tq, const CUtensorMap& tk,
-                          const CUtensorMap& tv, const Params& p) {
-  auto* kern = attn_fwd_kernel<kPingPong, kEmu, kProf, kDual>;
+// Tensor maps of one call: Q and V in 64-column x 128-row boxes; K in 128-row boxes (1-SM form)
+// or 64-row boxes (pair form: each SM stages half of a K tile).
+struct Maps {
+  CUtensorMap q, k, k_half, v;
+};
+
+template <bool kPair, uint32_t kEmuMask, uint32_t kEmuChunks, int kSplit, bool kPingPong, bool kProf>
+static int launch_variant(cudaStream_t st, const Maps& m, const Params& p) {
+  auto* kern = attn_fwd_kernel<kPair, kEmuMask, kEmuChunks, kSplit, kPingPong, kProf>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) != cudaSuccess)
     return H3_ERR_LAUNCH;
-  kern<<<grid, kThreads, kSmemBytes, st>>>(tq, tk, tv, p);
+  // one CTA per 256 query rows; the pair form launches whole two-CTA clusters (512 rows each)
+  const unsigned ctas = kPair ? 2u * unsigned((p.s_q + 2 * kRowsPerCta - 1) / (2 * kRowsPerCta))
+                              : unsigned((p.s_q + kRowsPerCta - 1) / kRowsPerCta);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ctas, (unsigned)p.n_heads);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kPair ? 2 : 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, m.q, kPair ? m.k_half : m.k, m.v, p) != cudaSuccess) return H3_ERR_LAUNCH;
   return cudaGetLastError() == cudaSuccess ? H3_OK : H3_ERR_LAUNCH;
+}
+
+// Schedule variants: (SM-pair MMAs, FMA-pipe exp2 pair positions in a 32-key chunk, chunks that
+// use them, P hand-off after kSplit of the 4 chunks, softmax ping-pong). Variants with the same
+// exp2 placement compute bit-identical results.
+template <bool kProf>
+static int launch_schedule(int variant, cudaStream_t st, const Maps& m, const Params& p) {
+  switch (variant) {
+    case 0: return launch_variant<false, 0x0000u, 0x0u, 3, false, kProf>(st, m, p);
+    case 1: return launch_variant<true, 0x0000u, 0x0u, 3, false, kProf>(st, m, p);
+    case 2: return launch_variant<true, 0x4444u, 0x6u, 3, false, kProf>(st, m, p);
+    case 3: return launch_variant<true, 0x4444u, 0x7u, 3, false, kProf>(st, m, p);
+    case 4: return launch_variant<true, 0x5555u, 0x6u, 3, false, kProf>(st, m, p);
+    case 5: return launch_variant<true, 0x0000u, 0x0u, 2, false, kProf>(st, m, p);
+    case 6: return launch_variant<false, 0x4444u, 0x6u, 3, false, kProf>(st, m, p);
+    case 7: return launch_variant<true, 0x0444u, 0x7u, 3, false, kProf>(st, m, p);
+    case 8: return launch_variant<true, 0x5555u, 0x7u, 3, false, kProf>(st, m, p);
+    default: return H3_ERR_UNSUPPORTED;
+  }
 }
 
 constexpr int kDefaultVariant = 0;
@@ -800,11 +926,13 @@ static int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, i
 
   const long long qhs = n_heads > 1 ? q_head_stride : s_q * q_row_stride;
   const long long kvhs = n_heads > 1 ? kv_head_stride : s_kv * kv_row_stride;
-  CUtensorMap tq, tk, tv;
+  // K maps: whole 128-key tiles (1-SM form) and 64-key halves (each SM of the pair form)
+  Maps m;
   int rc;
-  if ((rc = make_head_map(&tq, q, s_q, n_heads, q_row_stride, qhs)) != H3_OK) return rc;
-  if ((rc = make_head_map(&tk, k, s_kv, n_heads, kv_row_stride, kvhs)) != H3_OK) return rc;
-  if ((rc = make_head_map(&tv, v, s_kv, n_heads, kv_row_stride, kvhs)) != H3_OK) return rc;
+  if ((rc = make_head_map(&m.q, q, s_q, n_heads, q_row_stride, qhs)) != H3_OK) return rc;
+  if ((rc = make_head_map(&m.k, k, s_kv, n_heads, kv_row_stride, kvhs)) != H3_OK) return rc;
+  if ((rc = make_head_map(&m.k_half, k, s_kv, n_heads, kv_row_stride, kvhs, 64)) != H3_OK) return rc;
+  if ((rc = make_head_map(&m.v, v, s_kv, n_heads, kv_row_stride, kvhs)) != H3_OK) return rc;
 
   Params p;
   p.n_heads = (int)n_heads;
@@ -822,30 +950,9 @@ static int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, i
   p.prof_iters = prof_iters;
   p.o_peer = o_peer;
 
-  dim3 grid((unsigned)((s_q + kRowsPerCta - 1) / kRowsPerCta), (unsigned)n_heads);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (prof != nullptr) {
-    switch (variant) {
-      case 0: return launch_variant<false, 0, true>(grid, st, tq, tk, tv, p);
-      case 1: return launch_variant<true, 0, true>(grid, st, tq, tk, tv, p);
-      case 2: return launch_variant<true, 4, true>(grid, st, tq, tk, tv, p);
-      case 3: return launch_variant<true, 8, true>(grid, st, tq, tk, tv, p);
-      case 10: return launch_variant<false, 0, true, true>(grid, st, tq, tk, tv, p);
-      case 11: return launch_variant<true, 0, true, true>(grid, st, tq, tk, tv, p);
-      default: return H3_ERR_UNSUPPORTED;
-    }
-  }
-  switch (variant) {
-    case 0: return launch_variant<false, 0>(grid, st, tq, tk, tv, p);
-    case 1: return launch_variant<true, 0>(grid, st, tq, tk, tv, p);
-    case 2: return launch_variant<true, 4>(grid, st, tq, tk, tv, p);
-    case 3: return launch_variant<true, 8>(grid, st, tq, tk, tv, p);
-    case 4: return launch_variant<true, 2>(grid, st, tq, tk, tv, p);
-    case 10: return launch_variant<false, 0, false, true>(grid, st, tq, tk, tv, p);
-    case 11: return launch_variant<true, 0, false, true>(grid, st, tq, tk, tv, p);
-    case 12: return launch_variant<false, 8, false, true>(grid, st, tq, tk, tv, p);
-    default: return H3_ERR_UNSUPPORTED;
-  }
+  if (prof != nullptr) return launch_schedule<true>(variant, st, m, p);
+  return launch_schedule<false>(variant, st, m, p);
 }
 
 extern "C" int h3_attn_fwd_variant(const void* q, const void* k, const void* v, void* o, int64_t n_heads,

@@ -65,6 +65,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that may suspend the thread until the phase completes, for at most kSuspendHintNs:
+// a waiting warp then sleeps instead of spinning through issue slots that the working warps of
+// its SM sub-partition need. It returns as soon as the phase completes.
+constexpr uint32_t kSuspendHintNs = 1000000;  // 1 ms between checks of the abort flag / time limit
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "n"(kSuspendHintNs)
+      : "memory");
+  return ok != 0;
+}
+
 // Shared state a CTA uses to give up cleanly: `abort` lives in shared memory,
 // `status` is the caller's device status word (also read as a grid-wide abort),
 // `limit_ns` how long one wait may poll before it gives up.
@@ -74,24 +90,29 @@ struct WaitCtx {
   unsigned long long limit_ns = H3_WAIT_LIMIT_NS;
 };
 
+// After every unsuccessful (suspending) try: leave when the CTA aborted, another CTA failed the
+// call, or the wait outlived its limit.
+__device__ __forceinline__ bool wait_should_stop(const WaitCtx& ctx, uint64_t t0, int code) {
+  if (*ctx.abort) return true;
+  if (*reinterpret_cast<volatile int*>(ctx.status) != 0) {
+    *ctx.abort = 1;
+    return true;
+  }
+  if (globaltimer_ns() - t0 > ctx.limit_ns) {
+    atomicCAS(ctx.status, 0, code);
+    *ctx.abort = 1;
+    return true;
+  }
+  return false;
+}
+
 // Bounded wait on phase `parity` of `bar`. Returns false when the CTA must abort.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const WaitCtx& ctx, int code) {
   if (mbar_try_wait(bar, parity)) return true;
-  uint64_t t0 = globaltimer_ns();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0u) {
-      if (*ctx.abort) return false;
-      if (*reinterpret_cast<volatile int*>(ctx.status) != 0) {
-        *ctx.abort = 1;
-        return false;
-      }
-      if (globaltimer_ns() - t0 > ctx.limit_ns) {
-        atomicCAS(ctx.status, 0, code);
-        *ctx.abort = 1;
-        return false;
-      }
-    }
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (mbar_try_wait_sleep(bar, parity)) return true;
+    if (wait_should_stop(ctx, t0, code)) return false;
   }
 }
 
@@ -209,7 +230,42 @@ __device__ __forceinline__ void tmem_ld64_wait(uint32_t taddr, uint32_t (&r)[64]
       : "r"(taddr), "r"(taddr + 32u)
       : "memory");
 }
+// Two 32-column loads issued without waiting; tmem_ld64_wait_on() completes them. The wait
+// names the registers as in/out operands, so no use of them can be scheduled before it.
+__device__ __forceinline__ void tmem_ld64_nowait(uint32_t taddr, uint32_t (&r)[64]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%64];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, "
+      "%48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%65];\n"
+      : H3_R8(0), H3_R8(8), H3_R8(16), H3_R8(24), H3_R8(32), H3_R8(40), H3_R8(48), H3_R8(56)
+      : "r"(taddr), "r"(taddr + 32u)
+      : "memory");
+}
 #undef H3_R8
+#define H3_RW8(i) "+r"(r[i + 0]), "+r"(r[i + 1]), "+r"(r[i + 2]), "+r"(r[i + 3]), "+r"(r[i + 4]), \
+                  "+r"(r[i + 5]), "+r"(r[i + 6]), "+r"(r[i + 7])
+__device__ __forceinline__ void tmem_ld64_wait_on(uint32_t (&r)[64]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n"
+               : H3_RW8(0), H3_RW8(8), H3_RW8(16), H3_RW8(24), H3_RW8(32), H3_RW8(40), H3_RW8(48), H3_RW8(56)
+               :
+               : "memory");
+}
+#undef H3_RW8
+
+// Per-warpgroup register budgets (setmaxnreg): a warpgroup gives registers back to the
+// CTA's pool or takes more from it. The counts must fit the registers the CTA was launched
+// with (threads x registers per thread at launch).
+template <int kRegs>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(kRegs));
+}
+template <int kRegs>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(kRegs));
+}
 
 #define H3_W8(i) "r"(r[i + 0]), "r"(r[i + 1]), "r"(r[i + 2]), "r"(r[i + 3]), "r"(r[i + 4]), "r"(r[i + 5]), \
                  "r"(r[i + 6]), "r"(r[i + 7])
@@ -341,24 +397,24 @@ __device__ __forceinline__ bool mbar_try_wait_acq_cluster(uint32_t bar, uint32_t
       : "memory");
   return ok != 0;
 }
+__device__ __forceinline__ bool mbar_try_wait_acq_cluster_sleep(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "n"(kSuspendHintNs)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait with cluster-scope acquire (for barriers that peer CTAs arrive on).
 __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, const WaitCtx& ctx, int code) {
   if (mbar_try_wait_acq_cluster(bar, parity)) return true;
-  uint64_t t0 = globaltimer_ns();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait_acq_cluster(bar, parity)) return true;
-    if ((i & 255u) == 0u) {
-      if (*ctx.abort) return false;
-      if (*reinterpret_cast<volatile int*>(ctx.status) != 0) {
-        *ctx.abort = 1;
-        return false;
-      }
-      if (globaltimer_ns() - t0 > ctx.limit_ns) {
-        atomicCAS(ctx.status, 0, code);
-        *ctx.abort = 1;
-        return false;
-      }
-    }
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (mbar_try_wait_acq_cluster_sleep(bar, parity)) return true;
+    if (wait_should_stop(ctx, t0, code)) return false;
   }
 }
 // 3-D tile load into this CTA's shared memory whose completion is counted on an mbarrier that
@@ -390,30 +446,73 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t bar, uint16_t cta_mask)
 }
 
 // ---------------------------------------------------------------- math
-// 2^x on the FMA pipe (relieves MUFU): n = round(x) through the 1.5*2^23 shifter,
-// f = x - n in [-1/2, 1/2], 2^f by a degree-3 polynomial with minimax relative error
-// 7.5e-5 (Remez fit, csrc/gen_exp2_poly.py), n added straight into the exponent field.
-// x < -125 returns 0 (masked keys stay exactly zero; results stay normal numbers). The operation order is fixed,
-// so results do not depend on launch shape.
-__device__ __forceinline__ float ex2_poly(float x) {
-  const float shifter = 12582912.0f;  // 1.5 * 2^23
-  const float xc = fmaxf(x, -125.0f);
-  const float t = __fadd_rn(xc, shifter);
-  const float n = __fsub_rn(t, shifter);
-  const float f = __fsub_rn(xc, n);
-  float q = __fmaf_rn(5.517166853e-02f, f, 2.426111251e-01f);
-  q = __fmaf_rn(q, f, 6.932609677e-01f);
-  q = __fmaf_rn(q, f, 9.999280572e-01f);
-  const int ni = __float_as_int(t) - 0x4B400000;
-  const float r = __int_as_float(__float_as_int(q) + (ni << 23));
-  return x < -125.0f ? 0.0f : r;
-}
-
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// Packed fp32 pairs (sm_100 f32x2 ALU forms): each lane is an IEEE round-to-nearest
+// operation, identical to its scalar counterpart, at one issue slot per pair.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// max(a, b, c) in one instruction.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for a pair on the FMA pipe (relieves MUFU, which issues 16 exponentials per clock per
+// SM): x is clamped at -127, n = floor(x) comes from the 1.5*2^23 shifter added with
+// round-toward-minus-infinity, f = x - n lies in [0, 1), 2^f = 1 + c1 f + c2 f^2 + c3 f^3 with
+// minimax relative error 8.6e-5 (linear-programming fit, csrc/gen_exp2_poly.py), and n is added
+// straight into the exponent field: the shifter's low bits hold n, and shifting them up by 23
+// drops the shifter's own exponent bits. p(f) lies in [1, 2), so any n >= -127 leaves a valid
+// (at worst subnormal) fp32; x = -inf (a masked key) gives f = 0, p = 1 and exactly +0. Every
+// step is one IEEE-rounded operation in a fixed order, so results do not depend on launch shape.
+__device__ __forceinline__ void ex2_poly2(float x0, float x1, float& y0, float& y1) {
+  const uint64_t shifter = 0x4B4000004B400000ull;  // 1.5 * 2^23, twice
+  const uint64_t k3 = 0x3D9DD56E3D9DD56Eull;       // 7.706724107e-02f
+  const uint64_t k2 = 0x3E691BC43E691BC4ull;       // 2.276449800e-01f
+  const uint64_t k1 = 0x3F31F32A3F31F32Aull;       // 6.951166391e-01f
+  const uint64_t one = 0x3F8000003F800000ull;      // 1.0f
+  uint32_t r0, r1;
+  asm("{\n\t.reg .f32 a, b;\n\t.reg .b64 xc, t, n, f, q;\n\t.reg .b32 q0, q1, t0, t1;\n\t"
+      "max.f32 a, %2, 0fC2FE0000;\n\t"
+      "max.f32 b, %3, 0fC2FE0000;\n\t"
+      "mov.b64 xc, {a, b};\n\t"
+      "add.rm.f32x2 t, xc, %4;\n\t"
+      "sub.rn.f32x2 n, t, %4;\n\t"
+      "sub.rn.f32x2 f, xc, n;\n\t"
+      "fma.rn.f32x2 q, f, %5, %6;\n\t"
+      "fma.rn.f32x2 q, q, f, %7;\n\t"
+      "fma.rn.f32x2 q, q, f, %8;\n\t"
+      "mov.b64 {q0, q1}, q;\n\t"
+      "mov.b64 {t0, t1}, t;\n\t"
+      "mad.lo.u32 %0, t0, 8388608, q0;\n\t"
+      "mad.lo.u32 %1, t1, 8388608, q1;\n\t}\n"
+      : "=r"(r0), "=r"(r1)
+      : "f"(x0), "f"(x1), "l"(shifter), "l"(k3), "l"(k2), "l"(k1), "l"(one));
+  y0 = __uint_as_float(r0);
+  y1 = __uint_as_float(r1);
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);  // .x (low 16 bits) = lo
   return *reinterpret_cast<uint32_t*>(&v);

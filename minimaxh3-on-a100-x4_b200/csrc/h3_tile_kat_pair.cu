@@ -1,74 +1,12 @@
-// CTA-pair (2-SM) tile known-answer kernels: tcgen05.mma.cta_group::2 with
-// M = 256, where each CTA of the pair holds 128 rows of A and D and half of B (N/2).
-//   S = Q K^T: B = K split by keys (CTA r holds keys [64r, 64r+64) of the tile)
-//   O += P V : B = V split by head dimension (CTA r holds d in [64r, 64r+64))
-// This file holds the pair tile known-answer kernels (cf. attn_sm80/microtest.py:10-26): they
-// check the 2-SM MMA path (operand split, descriptors, TMEM layout) that the projection GEMM
-// builds on.
-#include "h3_ptx.cuh"
+// CTA-pair (2-SM) tile known-answer kernels (cf. attn_sm80/microtest.py:10-26): one pair
+// Q K^T and one pair P V tile through the same TMA / descriptor / tcgen05.mma.cta_group::2 path
+// that the attention kernel's pair form and the projection GEMM use (operand split per
+// h3_pair.cuh, TMEM layout).
+#include "h3_pair.cuh"
 #include "h3attn.h"
 
 namespace h3 {
 namespace pair {
-
-constexpr uint32_t kQTileBytes = 128u * 128u * 2u;  // 128 rows x 128 bf16 (two 64-column SW128 blocks)
-constexpr uint32_t kHalfK = 64u * 128u * 2u;        // 64 keys x 128 d (two 8 KB SW128 blocks)
-constexpr uint32_t kHalfV = 128u * 64u * 2u;        // 128 keys x 64 d (one SW128 block)
-
-// S (+)= Q K^T for the pair: A = this CTA's 128 Q rows (K-major, 64-column blocks 16 KB apart),
-// B = this CTA's 64 keys (K-major, 64-column blocks 8 KB apart). Issued by the leader only.
-__device__ __forceinline__ void issue_qk_pair(uint32_t d_tmem, uint32_t a_base, uint32_t b_base) {
-  constexpr uint32_t idesc = idesc_bf16_f32(256, 128, 0, 0);
-  const uint64_t ad = smem_desc_sw128(a_base, 16, 1024), bd = smem_desc_sw128(b_base, 16, 1024);
-  const uint32_t alo = uint32_t(ad), ahi = uint32_t(ad >> 32), blo = uint32_t(bd), bhi = uint32_t(bd >> 32);
-#define H3_QK2_STEP(OA, OB) \
-  "add.u32 la, %1, " #OA ";\n\t add.u32 lb, %3, " #OB ";\n\t" \
-  "mov.b64 da, {la, %2};\n\t mov.b64 db, {lb, %4};\n\t" \
-  "tcgen05.mma.cta_group::2.kind::f16 [%0], da, db, %5, pt;\n\t"
-  asm volatile(
-      "{\n\t.reg .pred pf, pt;\n\t.reg .b32 la, lb;\n\t.reg .b64 da, db;\n\t"
-      "setp.ne.b32 pf, %0, %0;\n\t setp.eq.b32 pt, %0, %0;\n\t"
-      "mov.b64 da, {%1, %2};\n\t mov.b64 db, {%3, %4};\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], da, db, %5, pf;\n\t"
-      H3_QK2_STEP(2, 2) H3_QK2_STEP(4, 4) H3_QK2_STEP(6, 6)
-      H3_QK2_STEP(1024, 512) H3_QK2_STEP(1026, 514) H3_QK2_STEP(1028, 516) H3_QK2_STEP(1030, 518)
-      "}\n" ::"r"(d_tmem), "r"(alo), "r"(ahi), "r"(blo), "r"(bhi), "r"(idesc)
-      : "memory");
-#undef H3_QK2_STEP
-}
-
-// O (+)= P V over 64 keys of the pair (half = 0: keys 0..63, 1: keys 64..127): P from TMEM
-// at p_tmem + p_half_cols*half (8 columns per 16-key step), V = this CTA's 64 d-columns of the 128-key
-// tile (MN-major, one SW128 block, 8-key groups 1 KB apart, 16-key steps 2 KB apart).
-__device__ __forceinline__ void issue_pv_pair(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_base, int half,
-                                              bool accumulate, uint32_t p_half_cols = 32) {
-  constexpr uint32_t idesc = idesc_bf16_f32(256, 128, 0, 1);
-  const uint64_t bd = smem_desc_sw128(v_base + uint32_t(half) * 4u * 2048u, kHalfV, 1024);
-  const uint32_t blo = uint32_t(bd), bhi = uint32_t(bd >> 32);
-  const uint32_t pa = p_tmem + uint32_t(half) * p_half_cols;
-#define H3_PV2_STEP(KK) \
-  "add.u32 ta, %1, " #KK "*8;\n\t add.u32 lb, %2, " #KK "*128;\n\t mov.b64 db, {lb, %3};\n\t" \
-  "tcgen05.mma.cta_group::2.kind::f16 [%0], [ta], db, %4, pt;\n\t"
-  asm volatile(
-      "{\n\t.reg .pred pf, pt;\n\t.reg .b32 ta, lb;\n\t.reg .b64 db;\n\t"
-      "setp.ne.b32 pf, %5, 0;\n\t setp.eq.b32 pt, %5, %5;\n\t"
-      "mov.b64 db, {%2, %3};\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], db, %4, pf;\n\t"
-      H3_PV2_STEP(1) H3_PV2_STEP(2) H3_PV2_STEP(3)
-      "}\n" ::"r"(d_tmem), "r"(pa), "r"(blo), "r"(bhi), "r"(idesc), "r"(accumulate ? 1u : 0u)
-      : "memory");
-#undef H3_PV2_STEP
-}
-
-__device__ __forceinline__ void drain_wait_pair(uint32_t bar, uint32_t parity, int* status) {
-  uint64_t t0 = globaltimer_ns();
-  while (!mbar_try_wait_acq_cluster(bar, parity)) {
-    if (globaltimer_ns() - t0 > H3_WAIT_LIMIT_NS) {
-      atomicCAS(status, 0, kStatusTimeoutDrain);
-      return;
-    }
-  }
-}
 
 // ---------------------------------------------------------------- pair KATs
 // S[256][128] fp32 = Q[256][128] . K[128][128]^T with CTA r holding Q rows [128r, 128r+128)
@@ -184,8 +122,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(128, 1)
     if (rank == 0) {
       if (mbar_wait_cluster(b_full, 0, ctx, kStatusTimeoutKat)) {
         tc_fence_after();
-        issue_pv_pair(tmem + 128, tmem + 64, sb, 0, false);
-        issue_pv_pair(tmem + 128, tmem + 64, sb, 1, true);
+        issue_pv_pair_steps<0, 8>(tmem + 128, tmem + 64, sb, false);
       }
       mma_commit_pair(b_done, 0x3);
     }
