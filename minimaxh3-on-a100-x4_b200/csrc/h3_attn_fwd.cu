@@ -30,25 +30,31 @@ constexpr int kBlockN = 128;
 constexpr int kRowsPerCta = 2 * kBlockM;
 constexpr int kStages = 5;  // K/V ring of whole tiles: the MMA thread waits for V_j and K_{j+1} a full iteration ahead
 constexpr int kMaxRing = 2 * kStages;  // the pair form's ring of half tiles (same bytes)
+// Ring stages are handed back through kRel release barriers used round robin: release r
+// completes once S_1(r) is ready, i.e. once every MMA reading K_r and V_(r-1) has retired.
+// A parity wait is safe while the producer trails by at most one phase of the barrier it
+// waits on; it has loaded at most kRing - 1 items beyond the ones release e frees, and release
+// e + kRel needs item 2(e + kRel), so kRel >= kMaxRing / 2 keeps every wait within one phase.
+constexpr int kRel = kMaxRing / 2;
 constexpr uint32_t kHalfBytes = 128u * 64u * 2u;  // 128 rows x 64 bf16: one 128-B swizzle column block
 constexpr uint32_t kTileBytes = 2u * kHalfBytes;  // 128 rows x 128 bf16
 constexpr int kThreads = 384;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 // Register budgets after the set-up: the producer / MMA / allocator warpgroup needs few, the two
-// softmax warpgroups hold a 128-score row each. 128 * 56 + 256 * 224 = 384 * 168, the launch's total.
+// softmax warpgroups hold a 128-score row each. 128 * 72 + 256 * 216 = 384 * 168, the launch's total.
 constexpr int kRegsLaunch = 168;
-constexpr int kRegsControl = 56;
-constexpr int kRegsSoftmax = 224;
+constexpr int kRegsControl = 72;
+constexpr int kRegsSoftmax = 216;
 static_assert(128 * kRegsControl + 256 * kRegsSoftmax <= kThreads * kRegsLaunch, "register split over budget");
 
 enum Bar : int {
   kBarQFull = 0,
   kBarKVFull = 1,
-  kBarKVEmpty = kBarKVFull + kMaxRing,
-  kBarSFull = kBarKVEmpty + kMaxRing,  // S_t ready (per Q tile)
+  kBarRel = kBarKVFull + kMaxRing,    // ring releases, round robin (see kRel)
+  kBarSFull = kBarRel + kRel,         // S_t ready (per Q tile)
   kBarPSplit = kBarSFull + 2,          // P_t chunks [0, kSplit) in TMEM
   kBarPLast = kBarPSplit + 2,          // all of P_t in TMEM
-  kBarODone = kBarPLast + 2,           // P_t * V retired
+  kBarODone = kBarPLast + 2,           // the last P_t * V retired
   kBarDrain = kBarODone + 2,
   kBarTok = kBarDrain + 1,  // softmax ping-pong token, one per warpgroup
   kNumBars = kBarTok + 2
@@ -229,10 +235,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(bar(kBarQFull), 1);
-    for (int s = 0; s < kRing; ++s) {
-      mbar_init(bar(kBarKVFull + s), 1);
-      mbar_init(bar(kBarKVEmpty + s), 1);
-    }
+    for (int s = 0; s < kRing; ++s) mbar_init(bar(kBarKVFull + s), 1);
+    for (int r = 0; r < kRel; ++r) mbar_init(bar(kBarRel + r), 1);
     for (int t = 0; t < 2; ++t) {
       mbar_init(bar(kBarSFull + t), 1);
       mbar_init(bar(kBarPSplit + t), kPCount);
@@ -291,10 +295,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           bool ok = true;
           for (int kv = 0; kv < 2; ++kv, ++it) {
             const int st = it % kRing;
-            const uint32_t ph = uint32_t(it / kRing) & 1u;
-            if (!mbar_wait(bar(kBarKVEmpty + st), ph ^ 1u, ctx, kStatusTimeoutKV)) {
-              ok = false;
-              break;
+            if (it >= kRing) {
+              // the stage's previous item (it - kRing) is free once release e has completed:
+              // K_r (item 2r) after S_1(r), V_r (item 2r + 1) after S_1(r + 1)
+              const int e = (it - kRing + 1) / 2;
+              if (!mbar_wait(bar(kBarRel + e % kRel), uint32_t(e / kRel) & 1u, ctx, kStatusTimeoutKV)) {
+                ok = false;
+                break;
+              }
             }
             const uint32_t dst = skv + st * kStage;
             if constexpr (kPair) {
@@ -334,31 +342,60 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     } else if (warp == 1) {
       // ------------------------------------------------------------ MMA issuer (even CTA)
-      if (lane == 0 && leader && !grid_aborted) {
+      // The whole warp runs the loop and agrees on every wait; one elected lane issues the MMAs
+      // and commits.
+      if (leader && !grid_aborted) {
+        const bool issuer = elect_one();
         const uint32_t sq = sbase + kOffQ;
         const uint32_t skv = sbase + kOffKV;
-        const bool rec = blockIdx.x == 0 && blockIdx.y == 0;
+        const bool rec = blockIdx.x == 0 && blockIdx.y == 0 && issuer;
         // waits on barriers that the other CTA's threads or copies complete take cluster scope
         auto wait_x = [&](uint32_t b, uint32_t par, int code) -> bool {
+          bool got;
           if constexpr (kPair)
-            return mbar_wait_cluster(b, par, ctx, code);
+            got = mbar_wait_cluster(b, par, ctx, code);
           else
-            return mbar_wait(b, par, ctx, code);
+            got = mbar_wait(b, par, ctx, code);
+          return __all_sync(0xffffffffu, got);
         };
         auto wait_full = [&](int st_it) -> bool {
           return wait_x(bar(kBarKVFull + st_it % kRing), uint32_t(st_it / kRing) & 1u, kStatusTimeoutKV);
         };
         auto commit = [&](int b) {
-          if constexpr (kPair)
-            mma_commit_pair(bar(b), 0x3);
-          else
-            mma_commit(bar(b));
+          if (issuer) {
+            if constexpr (kPair)
+              mma_commit_pair(bar(b), 0x3);
+            else
+              mma_commit(bar(b));
+          }
+          __syncwarp();
         };
         auto qk = [&](int t, uint32_t k_base) {
-          if constexpr (kPair)
-            pair::issue_qk_pair(tmem + col_s(t), sq + t * kTileBytes, k_base);
-          else
-            issue_qk(tmem + col_s(t), sq + t * kTileBytes, k_base);
+          if (issuer) {
+            if constexpr (kPair)
+              pair::issue_qk_pair(tmem + col_s(t), sq + t * kTileBytes, k_base);
+            else
+              issue_qk(tmem + col_s(t), sq + t * kTileBytes, k_base);
+          }
+          __syncwarp();
+        };
+        auto pv_head = [&](int t, uint32_t v_base, bool acc) {
+          if (issuer) {
+            if constexpr (kPair)
+              pair::issue_pv_pair_steps<0, 2 * kSplit>(tmem + col_o(t), tmem + col_p(t), v_base, acc);
+            else
+              issue_pv_steps<0, 2 * kSplit>(tmem + col_o(t), tmem + col_p(t), v_base, acc);
+          }
+          __syncwarp();
+        };
+        auto pv_tail = [&](int t, uint32_t v_base) {
+          if (issuer) {
+            if constexpr (kPair)
+              pair::issue_pv_pair_steps<2 * kSplit, 8 - 2 * kSplit>(tmem + col_o(t), tmem + col_p(t), v_base, true);
+            else
+              issue_pv_steps<2 * kSplit, 8 - 2 * kSplit>(tmem + col_o(t), tmem + col_p(t), v_base, true);
+          }
+          __syncwarp();
         };
         bool ok = wait_x(bar(kBarQFull), 0, kStatusTimeoutQ) && wait_full(0);
         if (ok) {
@@ -367,7 +404,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           commit(kBarSFull + 0);
           qk(1, skv);
           commit(kBarSFull + 1);
-          commit(kBarKVEmpty + 0);
         }
         for (int j = 0; ok && j < n_kv; ++j) {
           prof_mark<kProf>(p, rec, 2, j, 0);
@@ -384,36 +420,33 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!(ok = wait_x(bar(kBarPSplit + t), ph, kStatusTimeoutP))) break;
             prof_mark<kProf>(p, rec, 2, j, 2 + 3 * t);
             tc_fence_after();
-            if constexpr (kPair)
-              pair::issue_pv_pair_steps<0, 2 * kSplit>(tmem + col_o(t), tmem + col_p(t), sv, j > 0);
-            else
-              issue_pv_steps<0, 2 * kSplit>(tmem + col_o(t), tmem + col_p(t), sv, j > 0);
+            pv_head(t, sv, j > 0);
             if (!(ok = wait_x(bar(kBarPLast + t), ph, kStatusTimeoutP))) break;
             prof_mark<kProf>(p, rec, 2, j, 3 + 3 * t);
             tc_fence_after();
-            if constexpr (kPair)
-              pair::issue_pv_pair_steps<2 * kSplit, 8 - 2 * kSplit>(tmem + col_o(t), tmem + col_p(t), sv, true);
-            else
-              issue_pv_steps<2 * kSplit, 8 - 2 * kSplit>(tmem + col_o(t), tmem + col_p(t), sv, true);
-            commit(kBarODone + t);
-            if (t == 1) commit(kBarKVEmpty + it_v % kRing);
+            pv_tail(t, sv);
+            // every tcgen05.commit drains the tensor pipe (~100 clk), so a tile commits once per
+            // iteration (S ready, which also certifies its P V) and O only after the last P V
+            if (!next) commit(kBarODone + t);
             if (next) {
               if (t == 0 && !(ok = wait_full(it_k))) break;  // overlaps the queued P*V work
               qk(t, sk);
               commit(kBarSFull + t);
-              if (t == 1) commit(kBarKVEmpty + it_k % kRing);
             }
             prof_mark<kProf>(p, rec, 2, j, 4 + 3 * t);
           }
         }
         // Every issued MMA must retire before TMEM is released.
-        if constexpr (kPair) {
-          mma_commit_pair(bar(kBarDrain), 0x1);
-          pair::drain_wait_pair(bar(kBarDrain), 0, p.status);
-        } else {
-          mma_commit(bar(kBarDrain));
-          drain_wait(bar(kBarDrain), 0, p.status);
+        if (issuer) {
+          if constexpr (kPair) {
+            mma_commit_pair(bar(kBarDrain), 0x1);
+            pair::drain_wait_pair(bar(kBarDrain), 0, p.status);
+          } else {
+            mma_commit(bar(kBarDrain));
+            drain_wait(bar(kBarDrain), 0, p.status);
+          }
         }
+        __syncwarp();
       }
     }
   } else {
@@ -449,6 +482,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       prof_mark<kProf>(p, rec, t, j, 0);
       ok = __all_sync(0xffffffffu, mbar_wait(bar(kBarSFull + t), uint32_t(j) & 1u, ctx, kStatusTimeoutS));
       if (!ok) break;
+      // S_1(j) ready: every MMA reading K_j and V_(j-1) has retired; hand their stages back
+      if (t == 1 && quad == 0 && lane == 0) mbar_arrive(bar(kBarRel + j % kRel));
       prof_mark<kProf>(p, rec, t, j, 1);
       tc_fence_after();
       // S in two 64-column halves: the second half's load is in flight while the first half's
@@ -563,7 +598,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float l_run = (la0 + la1) + (lb0 + lb1);
     if (ok) {
       ok = __all_sync(0xffffffffu,
-                      mbar_wait(bar(kBarODone + t), uint32_t(n_kv - 1) & 1u, ctx, kStatusTimeoutO));
+                      mbar_wait(bar(kBarODone + t), 0, ctx, kStatusTimeoutO));
     }
     // Peer outputs (o_peer) are staged in this tile's Q buffer (its last Q*K^T has retired) and
     // stored as whole 256-byte rows, 16 threads per row, so every warp store writes two contiguous

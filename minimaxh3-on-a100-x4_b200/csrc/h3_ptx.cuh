@@ -116,6 +116,20 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const W
   }
 }
 
+// One lane of a converged warp (elect.sync). A single-thread instruction stream inside a warp
+// that runs the same loop on all lanes: an MMA-issuing loop written this way keeps the tensor
+// pipe fed while other warps of the SM sub-partition issue at full rate, where a lane-0-only
+// branch falls behind.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(r));
+  return r != 0;
+}
+
 // ---------------------------------------------------------------- TMA (plain, per CTA)
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
