@@ -276,20 +276,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0) {
       // ------------------------------------------------------------ TMA producer
       // Ring order K_0, V_0, K_1, V_1, ...; in the pair form each CTA loads its halves and the
-      // copies of both CTAs count on the even CTA's full barriers.
-      if (lane == 0 && !grid_aborted) {
+      // copies of both CTAs count on the even CTA's full barriers. The whole warp runs the loop
+      // and agrees on every wait; one elected lane issues the copies.
+      if (!grid_aborted) {
+        const bool issuer = elect_one();
         const uint32_t sq = sbase + kOffQ;
         const uint32_t skv = sbase + kOffKV;
-        const uint32_t q_full = kPair ? mapa_shared(bar(kBarQFull), 0) : bar(kBarQFull);
-        if (leader) mbar_expect_tx(bar(kBarQFull), (kPair ? 4 : 2) * kTileBytes);
-        for (int t = 0; t < 2; ++t)
-          for (int hh = 0; hh < 2; ++hh) {
-            if constexpr (kPair)
-              tma_load_3d_pair(sq + t * kTileBytes + hh * kHalfBytes, &tmap_q, q_full, hh * 64, m0 + t * kBlockM,
-                               head);
-            else
-              tma_load_3d(sq + t * kTileBytes + hh * kHalfBytes, &tmap_q, q_full, hh * 64, m0 + t * kBlockM, head);
-          }
+        if (issuer) {
+          const uint32_t q_full = kPair ? mapa_shared(bar(kBarQFull), 0) : bar(kBarQFull);
+          if (leader) mbar_expect_tx(bar(kBarQFull), (kPair ? 4 : 2) * kTileBytes);
+          for (int t = 0; t < 2; ++t)
+            for (int hh = 0; hh < 2; ++hh) {
+              if constexpr (kPair)
+                tma_load_3d_pair(sq + t * kTileBytes + hh * kHalfBytes, &tmap_q, q_full, hh * 64, m0 + t * kBlockM,
+                                 head);
+              else
+                tma_load_3d(sq + t * kTileBytes + hh * kHalfBytes, &tmap_q, q_full, hh * 64, m0 + t * kBlockM, head);
+            }
+        }
+        __syncwarp();
         int it = 0;
         for (int j = 0; j < n_kv; ++j) {
           bool ok = true;
@@ -299,34 +304,38 @@ __global__ void __launch_bounds__(kThreads, 1)
               // the stage's previous item (it - kRing) is free once release e has completed:
               // K_r (item 2r) after S_1(r), V_r (item 2r + 1) after S_1(r + 1)
               const int e = (it - kRing + 1) / 2;
-              if (!mbar_wait(bar(kBarRel + e % kRel), uint32_t(e / kRel) & 1u, ctx, kStatusTimeoutKV)) {
+              if (!__all_sync(0xffffffffu,
+                              mbar_wait(bar(kBarRel + e % kRel), uint32_t(e / kRel) & 1u, ctx, kStatusTimeoutKV))) {
                 ok = false;
                 break;
               }
             }
             const uint32_t dst = skv + st * kStage;
-            if constexpr (kPair) {
-              const uint32_t full = mapa_shared(bar(kBarKVFull + st), 0);
-              if (leader) mbar_expect_tx(bar(kBarKVFull + st), kTileBytes);
-              if (kv == 0) {  // K: this CTA's 64 keys, both 64-column blocks (64-row boxes)
-                for (int hh = 0; hh < 2; ++hh)
-                  tma_load_3d_pair(dst + hh * (kStage / 2), &tmap_k, full, hh * 64, j * kBlockN + 64 * int(rank),
-                                   head);
-              } else {  // V: all 128 keys, this CTA's 64 head-dimension columns
-                tma_load_3d_pair(dst, &tmap_v, full, 64 * int(rank), j * kBlockN, head);
+            if (issuer) {
+              if constexpr (kPair) {
+                const uint32_t full = mapa_shared(bar(kBarKVFull + st), 0);
+                if (leader) mbar_expect_tx(bar(kBarKVFull + st), kTileBytes);
+                if (kv == 0) {  // K: this CTA's 64 keys, both 64-column blocks (64-row boxes)
+                  for (int hh = 0; hh < 2; ++hh)
+                    tma_load_3d_pair(dst + hh * (kStage / 2), &tmap_k, full, hh * 64, j * kBlockN + 64 * int(rank),
+                                     head);
+                } else {  // V: all 128 keys, this CTA's 64 head-dimension columns
+                  tma_load_3d_pair(dst, &tmap_v, full, 64 * int(rank), j * kBlockN, head);
+                }
+              } else {
+                const CUtensorMap* m = kv ? &tmap_v : &tmap_k;
+                mbar_expect_tx(bar(kBarKVFull + st), kTileBytes);
+                tma_load_3d(dst, m, bar(kBarKVFull + st), 0, j * kBlockN, head);
+                tma_load_3d(dst + kHalfBytes, m, bar(kBarKVFull + st), 64, j * kBlockN, head);
               }
-            } else {
-              const CUtensorMap* m = kv ? &tmap_v : &tmap_k;
-              mbar_expect_tx(bar(kBarKVFull + st), kTileBytes);
-              tma_load_3d(dst, m, bar(kBarKVFull + st), 0, j * kBlockN, head);
-              tma_load_3d(dst + kHalfBytes, m, bar(kBarKVFull + st), 64, j * kBlockN, head);
             }
+            __syncwarp();
           }
           if (!ok) break;
         }
         // Every issued copy must land before the CTA may exit (the pair's copies all count on the
         // even CTA's barriers; the odd CTA cannot leave before the final cluster barrier).
-        if (leader) {
+        if (leader && issuer) {
           auto drain = [&](uint32_t b, uint32_t par) {
             if constexpr (kPair)
               pair::drain_wait_pair(b, par, p.status);
@@ -339,6 +348,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (cnt > 0) drain(bar(kBarKVFull + st), uint32_t(cnt - 1) & 1u);
           }
         }
+        __syncwarp();
       }
     } else if (warp == 1) {
       // ------------------------------------------------------------ MMA issuer (even CTA)
@@ -926,13 +936,13 @@ static int launch_schedule(int variant, cudaStream_t st, const Maps& m, const Pa
   switch (variant) {
     case 0: return launch_variant<false, 0x0000u, 0x0u, 3, false, kProf>(st, m, p);
     case 1: return launch_variant<true, 0x0000u, 0x0u, 3, false, kProf>(st, m, p);
-    case 2: return launch_variant<true, 0x4444u, 0x6u, 3, false, kProf>(st, m, p);
-    case 3: return launch_variant<true, 0x4444u, 0x7u, 3, false, kProf>(st, m, p);
-    case 4: return launch_variant<true, 0x5555u, 0x6u, 3, false, kProf>(st, m, p);
-    case 5: return launch_variant<true, 0x0000u, 0x0u, 2, false, kProf>(st, m, p);
+    case 2: return launch_variant<false, 0x0000u, 0x0u, 2, false, kProf>(st, m, p);
+    case 3: return launch_variant<false, 0x0000u, 0x0u, 3, true, kProf>(st, m, p);
+    case 4: return launch_variant<false, 0x5555u, 0x6u, 3, false, kProf>(st, m, p);
+    case 5: return launch_variant<false, 0x1111u, 0x7u, 3, false, kProf>(st, m, p);
     case 6: return launch_variant<false, 0x4444u, 0x6u, 3, false, kProf>(st, m, p);
-    case 7: return launch_variant<true, 0x0444u, 0x7u, 3, false, kProf>(st, m, p);
-    case 8: return launch_variant<true, 0x5555u, 0x7u, 3, false, kProf>(st, m, p);
+    case 7: return launch_variant<false, 0x0000u, 0x0u, 4, false, kProf>(st, m, p);
+    case 8: return launch_variant<true, 0x5555u, 0x6u, 3, false, kProf>(st, m, p);
     default: return H3_ERR_UNSUPPORTED;
   }
 }

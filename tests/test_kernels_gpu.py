@@ -189,8 +189,8 @@ def test_bad_arguments_rejected(cuda_dev):
 # schedule variant -> (FMA-pipe exp2 pair positions in a 32-key chunk, chunks using them). Variants
 # with the same placement run the same arithmetic (1-SM or SM-pair MMAs, another P hand-off) and
 # are bit-identical.
-VARIANT_EMU = {0: (0, 0), 1: (0, 0), 2: (0x4444, 6), 3: (0x4444, 7), 4: (0x5555, 6), 5: (0, 0),
-               6: (0x4444, 6), 7: (0x0444, 7), 8: (0x5555, 7)}
+VARIANT_EMU = {0: (0, 0), 1: (0, 0), 2: (0, 0), 3: (0, 0), 4: (0x5555, 6), 5: (0x1111, 7), 6: (0x4444, 6),
+               7: (0, 0), 8: (0x5555, 6)}
 
 
 @pytest.mark.parametrize("variant", sorted(VARIANT_EMU))
