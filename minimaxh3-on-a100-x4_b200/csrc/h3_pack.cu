@@ -64,10 +64,12 @@ __device__ __forceinline__ void norm_rope_row(const uint4& u0, const uint4& u1, 
 
 // One warp per token (grid-stride): the token's rotation table row (1 KB) is loaded into
 // registers once and reused for its q and k heads; the warp's four 8-lane groups walk the
-// token's 3*n_heads head rows, kRowsInFlight rows per group per step so that many 16-byte
-// load pairs per lane are in flight. v rows are copied unchanged. Every lane joins every shuffle (rows past
-// the end are clamped and not stored), so any n_heads works.
-constexpr int kRowsInFlight = 4;
+// token's 2*n_heads q/k head rows, kRowsInFlight rows per group per step so that many 16-byte
+// load pairs per lane are in flight, then copy its n_heads v rows unchanged (no arithmetic).
+// Every lane joins every shuffle of the q/k loop (rows past the end are clamped and not stored),
+// so any n_heads works.
+constexpr int kRowsInFlight = 2;
+constexpr int kVRowsInFlight = 4;
 
 __global__ void __launch_bounds__(256, 2) qknorm_rope_pack_kernel(
     const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v,
@@ -81,7 +83,17 @@ __global__ void __launch_bounds__(256, 2) qknorm_rope_pack_kernel(
   const int grp = lane >> 3;
   const long long warp_id = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const long long n_warps = ((long long)gridDim.x * blockDim.x) >> 5;
-  const int n_rows = 3 * n_heads;
+  const int n_qk = 2 * n_heads;
+  // destination of head row h of tensor `tensor` (0 q, 1 k, 2 v) for token `tok`: the destination
+  // rank's buffer (a peer's memory over NVLink) laid out [tensor][head][row], or one local send
+  // buffer addressed by rank / head strides
+  auto dst_row = [&](int tensor, int h, long long tok) -> __nv_bfloat16* {
+    return rank_base != nullptr
+               ? reinterpret_cast<__nv_bfloat16*>(rank_base[h / heads_per_rank]) + tensor * tensor_stride +
+                     (long long)(h % heads_per_rank) * out_head_stride + (row_offset + tok) * kD
+               : (tensor == 0 ? q_out : (tensor == 1 ? k_out : v_out)) + (long long)(h / heads_per_rank) * out_rank_stride +
+                     (long long)(h % heads_per_rank) * out_head_stride + tok * kD;
+  };
   for (long long tok = warp_id; tok < s_l; tok += n_warps) {
     float4 m[8] = {};
     if (rope != nullptr) {
@@ -89,24 +101,24 @@ __global__ void __launch_bounds__(256, 2) qknorm_rope_pack_kernel(
 #pragma unroll
       for (int i = 0; i < 8; ++i) m[i] = __ldg(mr + i);
     }
-    for (int base = 0; base < n_rows; base += 4 * kRowsInFlight) {
+    for (int base = 0; base < n_qk; base += 4 * kRowsInFlight) {
       int rr[kRowsInFlight];
       uint4 u[kRowsInFlight][2];
 #pragma unroll
       for (int pr = 0; pr < kRowsInFlight; ++pr) {
         const int r = base + 4 * pr + grp;
         rr[pr] = r;
-        const int rc = r < n_rows ? r : n_rows - 1;
-        const int tensor = rc / n_heads, h = rc - tensor * n_heads;
-        const __nv_bfloat16* src = (tensor == 0 ? q : (tensor == 1 ? k : v)) + tok * in_row_stride + (long long)h * kD;
+        const int rc = r < n_qk ? r : n_qk - 1;
+        const int tensor = rc >= n_heads ? 1 : 0, h = rc - tensor * n_heads;
+        const __nv_bfloat16* src = (tensor == 0 ? q : k) + tok * in_row_stride + (long long)h * kD;
         u[pr][0] = __ldg(reinterpret_cast<const uint4*>(src + 8 * g));
         u[pr][1] = __ldg(reinterpret_cast<const uint4*>(src + 64 + 8 * g));
       }
 #pragma unroll
       for (int pr = 0; pr < kRowsInFlight; ++pr) {
         const int r = rr[pr];
-        const int rc = r < n_rows ? r : n_rows - 1;
-        const int tensor = rc / n_heads, h = rc - tensor * n_heads;
+        const int rc = r < n_qk ? r : n_qk - 1;
+        const int tensor = rc >= n_heads ? 1 : 0, h = rc - tensor * n_heads;
         uint4 o0, o1;
         float wsel[16];  // this row's RMSNorm weight (L1-resident), 1.0 when absent
         const __nv_bfloat16* w = tensor == 0 ? qw : kw;
@@ -117,24 +129,33 @@ __global__ void __launch_bounds__(256, 2) qknorm_rope_pack_kernel(
 #pragma unroll
           for (int i = 0; i < 16; ++i) wsel[i] = 1.0f;
         }
-        // v rows run the same (discarded) arithmetic so the warp stays converged for the shuffles
         norm_rope_row(u[pr][0], u[pr][1], wsel, m, rope != nullptr, eps, o0, o1);
-        if (tensor == 2) {
-          o0 = u[pr][0];
-          o1 = u[pr][1];
-        }
-        if (r < n_rows) {
-          // rank_base: the destination rank's buffer (a peer's memory over NVLink), laid out
-          // [tensor][head][row]; otherwise one local send buffer addressed by rank / head strides
-          __nv_bfloat16* dst =
-              rank_base != nullptr
-                  ? reinterpret_cast<__nv_bfloat16*>(rank_base[h / heads_per_rank]) + tensor * tensor_stride +
-                        (long long)(h % heads_per_rank) * out_head_stride + (row_offset + tok) * kD
-                  : (tensor == 0 ? q_out : (tensor == 1 ? k_out : v_out)) +
-                        (long long)(h / heads_per_rank) * out_rank_stride +
-                        (long long)(h % heads_per_rank) * out_head_stride + tok * kD;
+        if (r < n_qk) {
+          __nv_bfloat16* dst = dst_row(tensor, h, tok);
           reinterpret_cast<uint4*>(dst + 8 * g)[0] = o0;
           reinterpret_cast<uint4*>(dst + 64 + 8 * g)[0] = o1;
+        }
+      }
+    }
+    // v rows: copies, kVRowsInFlight per 8-lane group in flight
+    for (int base = 0; base < n_heads; base += 4 * kVRowsInFlight) {
+      uint4 u[kVRowsInFlight][2];
+#pragma unroll
+      for (int pr = 0; pr < kVRowsInFlight; ++pr) {
+        const int h = base + 4 * pr + grp;
+        if (h < n_heads) {
+          const __nv_bfloat16* src = v + tok * in_row_stride + (long long)h * kD;
+          u[pr][0] = __ldg(reinterpret_cast<const uint4*>(src + 8 * g));
+          u[pr][1] = __ldg(reinterpret_cast<const uint4*>(src + 64 + 8 * g));
+        }
+      }
+#pragma unroll
+      for (int pr = 0; pr < kVRowsInFlight; ++pr) {
+        const int h = base + 4 * pr + grp;
+        if (h < n_heads) {
+          __nv_bfloat16* dst = dst_row(2, h, tok);
+          reinterpret_cast<uint4*>(dst + 8 * g)[0] = u[pr][0];
+          reinterpret_cast<uint4*>(dst + 64 + 8 * g)[0] = u[pr][1];
         }
       }
     }
