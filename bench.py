@@ -25,6 +25,9 @@ Printed by rank 0 as ONE JSON line:
                  forward, max over ranks, its own clock record, per-category split; at N>1 also
                  bit-exact against the 1-GPU forward)
 
+--case <kernel> times one kernel of the path alone (attn, pack, gemm_qkv/out/fc1/fc2, norm_mod,
+residual) at --seq rows: the entry point of the profile summaries under profiles/.
+
 --impl reference times the reference's CPU path for this op (torch SDPA FLASH on the host
 cores, harness/sp_runtime.py:119-121) at config 0 (H=56, S=4096, fp32, seed 0).
 """
@@ -698,6 +701,72 @@ def forward_flops(s: int, blocks: int, hidden=5376, heads=56, head_dim=128, ffn=
     return blocks * (gemm + flops_layer(s, heads))
 
 
+# ----------------------------------------------------------------------------- single-kernel cases
+CASES = ("attn", "pack", "gemm_qkv", "gemm_out", "gemm_fc1", "gemm_fc2", "norm_mod", "residual")
+
+
+def run_case(args) -> None:
+    """One kernel of the path at a chosen size, for profiling (ncu -k <kernel> python bench.py --case ...):
+    `warmup` untimed launches, then `steps` launches timed with CUDA events; prints one JSON line with the
+    per-launch time and the kernel's rate against its roofline unit. Sizes: --seq rows (tokens), 56 heads,
+    hidden 5376, FFN 14336; inputs are seeded N(0, 1) (weights N(0, 0.02))."""
+    import h3attn
+    import h3_model
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    S, hidden, ffn = args.seq, 5376, 14336
+    rnd = lambda *shape, s=1.0: (torch.randn(shape, device=dev, generator=g) * s).to(torch.bfloat16)
+    if args.case == "attn":
+        q, k, v = (rnd(HEADS, S, D) for _ in range(3))
+        o = torch.empty_like(q)
+        fn = lambda: h3attn.attention(q, k, v, out=o)
+        work, unit = flops_layer(S), "TFLOP/s"
+    elif args.case == "pack":
+        x = rnd(S, 3 * HEADS * D)
+        rope = h3_model.rope_freqs_1d(S, device=dev)[0].contiguous()
+        ones = torch.ones(D, dtype=torch.bfloat16, device=dev)
+        q, k, v = x.split(HEADS * D, dim=-1)
+        fn = lambda: h3attn.qknorm_rope_pack(q, k, v, rope, ones, ones, 1e-6, 1)
+        work, unit = S * 3 * HEADS * D * 2 * 2 + S * 1024, "GB/s"
+    elif args.case.startswith("gemm_"):
+        k_in, n_out, ep = {"gemm_qkv": (hidden, 3 * HEADS * D, "none"), "gemm_out": (HEADS * D, hidden, "none"),
+                           "gemm_fc1": (hidden, 2 * ffn, "swiglu"), "gemm_fc2": (ffn, hidden, "none")}[args.case]
+        a, w = rnd(S, k_in), rnd(n_out, k_in, s=0.02)
+        out = h3attn.linear(a, w, epilogue=ep)
+        fn = lambda: h3attn.linear(a, w, out=out, epilogue=ep)
+        work, unit = 2.0 * S * k_in * n_out, "TFLOP/s"
+    else:
+        x, y = rnd(S, hidden), rnd(S, hidden)
+        mods = rnd(4, hidden, s=0.1)
+        seg = h3attn.segment_rows([(0, S // 2, 0), (S // 2, S, 1)], S, dev)
+        if args.case == "norm_mod":
+            xo, ho = torch.empty_like(x), torch.empty_like(x)
+            fn = lambda: h3attn.norm_modulate(x, mods[0:2], mods[2:4], seg, 1e-6, y=y, gate=mods[0:2], x_out=xo,
+                                              out=ho)
+            work = S * hidden * 2 * 4  # read x, y; write x_out, h
+        else:
+            ro = torch.empty_like(x)
+            fn = lambda: h3attn.gated_residual(x, y, mods[0:2], seg, out=ro)
+            work = S * hidden * 2 * 3  # read x, y; write out
+        unit = "GB/s"
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        fn()
+    ev1.record()
+    torch.cuda.synchronize()
+    h3attn.check_status()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    rate = work / (ms * 1e-3) / (1e12 if unit == "TFLOP/s" else 1e9)
+    print(json.dumps({"case": args.case, "rows": S, "ms_per_launch": ms, "achieved": rate, "unit": unit,
+                      "launches": args.steps}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -714,6 +783,8 @@ def main():
     ap.add_argument("--rb-blocks", type=int, default=50, help="config 3 run_blocks forward depth (0: skip)")
     ap.add_argument("--rb-seq", type=int, default=42000)
     ap.add_argument("--rb-steps", type=int, default=2, help="timed run_blocks forwards")
+    ap.add_argument("--case", choices=CASES, default=None,
+                    help="time one kernel of the path alone at --seq rows (profiling); 1 GPU, no JSON contract")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))
@@ -721,6 +792,9 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank, world)
+        return
+    if args.case is not None:
+        run_case(args)
         return
     torch.cuda.set_device(local)
     if world > 1:

@@ -43,60 +43,23 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-// Row statistics in one reduction: every thread holds (count, mean, M2) of its own values (a
-// two-pass sum in registers), and the pairs are merged with Chan's pairwise update
-//   n = na + nb, d = mb - ma, mean = ma + d * nb / n, M2 = M2a + M2b + d^2 * na * nb / n
-// in a fixed tree (shfl_down within warps, then over the warp results), so the order never
-// depends on timing. Numerically this is as robust as a two-pass variance.
-__device__ __forceinline__ void stats_merge(float& n, float& mean, float& m2, float nb, float mb, float m2b) {
-  if (nb == 0.f) return;
-  if (n == 0.f) {
-    n = nb;
-    mean = mb;
-    m2 = m2b;
-    return;
-  }
-  const float nt = n + nb;
-  const float d = mb - mean;
-  mean = mean + d * (nb / nt);
-  m2 = m2 + m2b + d * d * (n * nb / nt);
-  n = nt;
-}
-__device__ __forceinline__ void block_stats(float& n, float& mean, float& m2, float* red) {
+// Sum over the CTA; fixed order (warp butterfly, then warp 0 over the warp partials).
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float nb = __shfl_down_sync(0xffffffffu, n, o);
-    const float mb = __shfl_down_sync(0xffffffffu, mean, o);
-    const float m2b = __shfl_down_sync(0xffffffffu, m2, o);
-    if (lane + o < 32) stats_merge(n, mean, m2, nb, mb, m2b);
-  }
-  constexpr int kWarps = kThreads / 32;
-  if (lane == 0) {
-    red[warp] = n;
-    red[kWarps + warp] = mean;
-    red[2 * kWarps + warp] = m2;
-  }
+  if (lane == 0) red[warp] = v;
   __syncthreads();
+  float t = lane < kThreads / 32 ? red[lane] : 0.f;
   if (warp == 0) {
-    float wn = lane < kWarps ? red[lane] : 0.f;
-    float wm = lane < kWarps ? red[kWarps + lane] : 0.f;
-    float w2 = lane < kWarps ? red[2 * kWarps + lane] : 0.f;
 #pragma unroll
-    for (int o = kWarps / 2; o > 0; o >>= 1) {
-      const float nb = __shfl_down_sync(0xffffffffu, wn, o);
-      const float mb = __shfl_down_sync(0xffffffffu, wm, o);
-      const float m2b = __shfl_down_sync(0xffffffffu, w2, o);
-      if (lane + o < kWarps) stats_merge(wn, wm, w2, nb, mb, m2b);
-    }
-    if (lane == 0) {
-      red[3 * kWarps] = wm;
-      red[3 * kWarps + 1] = w2;
-    }
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (lane == 0) red[kThreads / 32] = t;
   }
   __syncthreads();
-  mean = red[3 * kWarps];
-  m2 = red[3 * kWarps + 1];
+  const float r = red[kThreads / 32];
+  __syncthreads();  // red is reused by the next call
+  return r;
 }
 
 struct NormParams {
@@ -121,12 +84,12 @@ struct NormParams {
 // registers, lets six rows per SM be in flight instead of four; 4 covers the rest.
 template <int kVec>
 __global__ void __launch_bounds__(kThreads, kVec == 3 ? 6 : 4) norm_modulate_kernel(const NormParams p) {
-  __shared__ float red[3 * (kThreads / 32) + 2];
+  __shared__ float red[kThreads / 32 + 1];
   const long long r = blockIdx.x;
   const int m = p.seg_row[r];
   const int n_vec = p.hidden >> 3;
   float v[kVec][8];
-  float s = 0.f, cnt = 0.f;
+  float s = 0.f;
 #pragma unroll
   for (int i = 0; i < kVec; ++i) {
     const int c = threadIdx.x + i * kThreads;
@@ -142,11 +105,9 @@ __global__ void __launch_bounds__(kThreads, kVec == 3 ? 6 : 4) norm_modulate_ker
       if (p.x_out != nullptr) *reinterpret_cast<uint4*>(p.x_out + r * p.x_out_stride + 8 * c) = pack8(v[i]);
 #pragma unroll
       for (int e = 0; e < 8; ++e) s += v[i][e];
-      cnt += 8.f;
     }
   }
-  // this thread's (count, mean, M2), then one block-wide merge
-  float mean = cnt > 0.f ? s / cnt : 0.f;
+  const float mean = block_sum(s, red) / float(p.hidden);
   float q = 0.f;
 #pragma unroll
   for (int i = 0; i < kVec; ++i) {
@@ -159,8 +120,7 @@ __global__ void __launch_bounds__(kThreads, kVec == 3 ? 6 : 4) norm_modulate_ker
       }
     }
   }
-  block_stats(cnt, mean, q, red);
-  const float rstd = rsqrtf(q / float(p.hidden) + p.eps);
+  const float rstd = rsqrtf(block_sum(q, red) / float(p.hidden) + p.eps);
 #pragma unroll
   for (int i = 0; i < kVec; ++i) {
     const int c = threadIdx.x + i * kThreads;

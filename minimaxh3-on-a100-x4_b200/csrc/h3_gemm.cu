@@ -31,10 +31,18 @@ constexpr int kStages = 6;
 constexpr uint32_t kTileBytes = 128u * 64u * 2u;  // 128 rows x 64 bf16 (one SW128 block)
 constexpr uint32_t kStageBytes = 2 * kTileBytes;  // A tile + W tile
 constexpr uint32_t kOffBars = kStages * kStageBytes;
+// Every tcgen05.commit drains the tensor pipe (~100 clk), against 512 clk of MMA work per k-block,
+// so ring stages are released kRelEvery k-blocks at a time: release e (one commit, reaching both
+// CTAs) frees the stages of k-blocks [kRelEvery e, kRelEvery e + kRelEvery). The producer waits
+// release (it - kStages) / kRelEvery before reusing a stage; release barriers are used round
+// robin, and with kRel > (kStages - 1) / kRelEvery every parity wait stays within one phase.
+constexpr int kRelEvery = 2;
+constexpr int kRel = 3;
+static_assert(kRel * kRelEvery > kStages - 1, "release barriers too few for the ring");
 enum : int {
   kFull = 0,                      // leader: both CTAs' A and W tiles of a stage landed
-  kEmpty = kFull + kStages,       // both: stage consumed (multicast commit)
-  kAccFull = kEmpty + kStages,    // both: accumulator b complete (multicast commit)
+  kRelease = kFull + kStages,     // both: k-block group consumed (multicast commit), round robin
+  kAccFull = kRelease + kRel,     // both: accumulator b complete (multicast commit)
   kAccEmpty = kAccFull + 2,       // leader: accumulator b drained by the epilogue warps of both CTAs
   kDrain = kAccEmpty + 2,         // leader: every issued MMA retired
   kNumBars = kDrain + 1
@@ -111,10 +119,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int n_clusters = gridDim.x >> 1;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(bar(kFull + s), 1);
-      mbar_init(bar(kEmpty + s), 1);
-    }
+    for (int s = 0; s < kStages; ++s) mbar_init(bar(kFull + s), 1);
+    for (int r = 0; r < kRel; ++r) mbar_init(bar(kRelease + r), 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(bar(kAccFull + b), 1);
       mbar_init(bar(kAccEmpty + b), 8);  // 4 epilogue warps in each CTA
@@ -140,7 +146,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer (both CTAs)
-    if (lane == 0 && !grid_aborted) {
+    // The whole warp runs the loop and agrees on every wait; one elected lane issues the copies.
+    if (!grid_aborted) {
+      const bool issuer = elect_one();
       int it = 0;
       bool ok = true;
       for (int t = cid; ok && t < p.n_tiles; t += n_clusters) {
@@ -150,45 +158,68 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int w_row = p.swiglu ? int(rank) * p.f + 128 * nb : nb * 256 + 128 * int(rank);
         for (int kb = 0; kb < p.n_kb; ++kb, ++it) {
           const int st = it % kStages;
-          if (!(ok = mbar_wait(bar(kEmpty + st), (uint32_t(it / kStages) & 1u) ^ 1u, ctx, kStatusTimeoutKV))) break;
-          if (rank == 0) mbar_expect_tx(bar(kFull + st), 2 * kStageBytes);
-          const uint32_t full_leader = mapa_shared(bar(kFull + st), 0);
-          const uint32_t dst = sbase + st * kStageBytes;
-          tma_load_3d_pair(dst, &tmap_a, full_leader, 64 * (kb % p.kc_blocks), a_row, kb / p.kc_blocks);
-          tma_load_3d_pair(dst + kTileBytes, &tmap_w, full_leader, 64 * kb, w_row, 0);
+          if (it >= kStages) {
+            const int e = (it - kStages) / kRelEvery;
+            if (!(ok = __all_sync(0xffffffffu, mbar_wait(bar(kRelease + e % kRel), uint32_t(e / kRel) & 1u, ctx,
+                                                        kStatusTimeoutKV))))
+              break;
+          }
+          if (issuer) {
+            if (rank == 0) mbar_expect_tx(bar(kFull + st), 2 * kStageBytes);
+            const uint32_t full_leader = mapa_shared(bar(kFull + st), 0);
+            const uint32_t dst = sbase + st * kStageBytes;
+            tma_load_3d_pair(dst, &tmap_a, full_leader, 64 * (kb % p.kc_blocks), a_row, kb / p.kc_blocks);
+            tma_load_3d_pair(dst + kTileBytes, &tmap_w, full_leader, 64 * kb, w_row, 0);
+          }
+          __syncwarp();
         }
       }
-      if (rank == 0) {
+      if (rank == 0 && issuer) {
         // every copy of both CTAs counts on the leader's barriers: drain them before exit
         for (int st = 0; st < kStages; ++st) {
           const int cnt = it / kStages + (st < it % kStages ? 1 : 0);
           if (cnt > 0) drain_wait_cluster(bar(kFull + st), uint32_t(cnt - 1) & 1u, p.status);
         }
       }
+      __syncwarp();
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (leader CTA)
-    if (rank == 0 && lane == 0 && !grid_aborted) {
+    // The whole warp runs the loop and agrees on every wait; one elected lane issues the MMAs and
+    // commits (a lane-0-only issuer falls behind when other warps issue at full rate).
+    if (rank == 0 && !grid_aborted) {
+      const bool issuer = elect_one();
       int it = 0, i = 0;
       bool ok = true;
       for (int t = cid; ok && t < p.n_tiles; t += n_clusters, ++i) {
         const int b = i & 1;
         // accumulator b is free once the epilogue drained the tile that used it two tiles ago
-        if (!(ok = mbar_wait_cluster(bar(kAccEmpty + b), (uint32_t(i >> 1) & 1u) ^ 1u, ctx, kStatusTimeoutO))) break;
+        if (!(ok = __all_sync(0xffffffffu, mbar_wait_cluster(bar(kAccEmpty + b), (uint32_t(i >> 1) & 1u) ^ 1u, ctx,
+                                                             kStatusTimeoutO))))
+          break;
         tc_fence_after();
         const uint32_t d = tmem + 256u * b;
         for (int kb = 0; kb < p.n_kb; ++kb, ++it) {
           const int st = it % kStages;
-          if (!(ok = mbar_wait_cluster(bar(kFull + st), uint32_t(it / kStages) & 1u, ctx, kStatusTimeoutKV))) break;
+          if (!(ok = __all_sync(0xffffffffu, mbar_wait_cluster(bar(kFull + st), uint32_t(it / kStages) & 1u, ctx,
+                                                               kStatusTimeoutKV))))
+            break;
           tc_fence_after();
           const uint32_t a_base = sbase + st * kStageBytes;
-          issue_kblock(d, a_base, a_base + kTileBytes, kb > 0);
-          mma_commit_pair(bar(kEmpty + st), 0x3);
+          if (issuer) {
+            issue_kblock(d, a_base, a_base + kTileBytes, kb > 0);
+            if (it % kRelEvery == kRelEvery - 1) mma_commit_pair(bar(kRelease + (it / kRelEvery) % kRel), 0x3);
+          }
+          __syncwarp();
         }
-        if (ok) mma_commit_pair(bar(kAccFull + b), 0x3);
+        if (ok && issuer) mma_commit_pair(bar(kAccFull + b), 0x3);
+        __syncwarp();
       }
-      mma_commit_pair(bar(kDrain), 0x1);
-      drain_wait_cluster(bar(kDrain), 0, p.status);
+      if (issuer) {
+        mma_commit_pair(bar(kDrain), 0x1);
+        drain_wait_cluster(bar(kDrain), 0, p.status);
+      }
+      __syncwarp();
     }
   } else {
     // ------------------------------------------------------------ epilogue (warps 2..5, both CTAs)
