@@ -159,23 +159,24 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- the CPU baseline
-def cpu_config0(reps: int, threads: int):
+def cpu_config0(reps: int, threads: int, warm: int = 1):
     """The reference's attention call (SDPA FLASH, sp_runtime.py:119-121) at config 0 (H=56,
-    S=4096, D=128, fp32, seed 0, RMSNorm + RoPE on q and k) on the host cores. One warm-up run,
+    S=4096, D=128, fp32, seed 0, RMSNorm + RoPE on q and k) on the host cores. `warm` warm-up runs,
     then `reps` timed runs; returns (per-run seconds, FLOPs per run, sample description)."""
     from oracle import north_star, sdpa_ref
     torch.set_num_threads(threads)
     H, S = 56, 4096
     q, k, v = north_star.config_inputs(0, H, S, "cpu")
     q, k, v = q[None], k[None], v[None]
-    sdpa_ref.attention(q, k, v)  # warm-up
+    for _ in range(warm):
+        sdpa_ref.attention(q, k, v)
     times = []
     for _ in range(reps):
         t0 = time.perf_counter()
         sdpa_ref.attention(q, k, v)
         times.append(time.perf_counter() - t0)
     sample = (f"config 0: B=1 H={H} S={S} D=128 fp32 seed 0 (RMSNorm + RoPE), the reference's SDPA FLASH call "
-              f"on the CPU, {threads} threads, median of {reps} after one warm-up")
+              f"on the CPU, {threads} threads, median of {reps} after {warm} warm-up run(s)")
     return times, flops_layer(S, H), sample
 
 
@@ -183,8 +184,7 @@ def run_reference(args, rank: int, world: int) -> None:
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    times, fl, sample = cpu_config0(args.warmup + args.steps, threads)
-    times = times[args.warmup:]
+    times, fl, sample = cpu_config0(args.steps, threads, warm=args.warmup)
     per = statistics.median(times)
     val = fl / per / 1e12
     line = {
