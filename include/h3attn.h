@@ -75,15 +75,16 @@ int h3_attn_fwd(const void* q, const void* k, const void* v, void* o, int64_t n_
 
 /* h3_attn_fwd with an explicit kernel schedule (a tuning hook; h3_attn_fwd uses the
  * default). All variants compute the same attention within the same tolerance; variants with
- * the same exp2 placement are bit-identical to each other (0, 1, 5 | 2, 6):
+ * the same exp2 placement are bit-identical to each other (0, 1, 2, 3, 7 | 4, 8):
  *   0  one CTA per SM, exp2 on MUFU, P handed over after 3 of its 4 32-key chunks (the default)
  *   1  SM pairs: tcgen05 cta_group::2 MMAs over two CTAs on two SMs, each staging half of every
  *      K and V tile; otherwise as 0
- *   2  as 1 with key pairs 2, 6, 10, 14 of 32-key chunks 1-2 on the FMA pipe (a degree-3
- *      polynomial exp2); 3 the same in chunks 0-2; 4 every other pair of chunks 1-2;
- *      7 pairs 2, 6, 10 of chunks 0-2; 8 every other pair of chunks 0-2
- *   5  as 1 with P handed over after 2 of 4 chunks
- *   6  as 0 with the exp2 placement of 2
+ *   2  as 0 with P handed over after 2 of 4 chunks; 7 the same after all 4
+ *   3  as 0 with the two softmax warpgroups taking turns for their exponentials
+ *   4  as 0 with every other key pair of 32-key chunks 1-2 on the FMA pipe (a degree-3
+ *      polynomial exp2); 5 key pairs 0, 4, 8, 12 of chunks 0-2; 6 key pairs 2, 6, 10, 14 of
+ *      chunks 1-2
+ *   8  as 1 with the exp2 placement of 4
  * Returns H3_ERR_UNSUPPORTED for any other value. */
 int h3_attn_fwd_variant(const void* q, const void* k, const void* v, void* o, int64_t n_heads, int64_t s_q,
                         int64_t s_kv, int64_t q_head_stride, int64_t q_row_stride, int64_t kv_head_stride,
