@@ -9,8 +9,9 @@
 // with LN = (x - mean) / sqrt(var + eps) in fp32 (biased variance, no affine), rounded to bf16.
 // h3_norm_modulate optionally applies a gated residual first and normalises its result (the
 // attention residual fused with norm2), so the block needs three passes over [rows][hidden].
-// One CTA per token row: the row (hidden <= 8192) stays in registers between the statistics and
-// the output; 16-byte loads and stores; every row is computed independently of the others.
+// One CTA per token row: the row (hidden <= 8192) stays in registers (as bf16) between the
+// statistics and the output; 16-byte loads and stores; every row is computed independently of the
+// others.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -80,31 +81,47 @@ struct NormParams {
   float eps;
 };
 
-// kVec vectors of 8 per thread hold the row: 3 covers hidden <= 6144 (H3's 5376) and, with fewer
-// registers, lets six rows per SM be in flight instead of four; 4 covers the rest.
-template <int kVec>
-__global__ void __launch_bounds__(kThreads, kVec == 3 ? 6 : 4) norm_modulate_kernel(const NormParams p) {
+// kVec vectors of 8 per thread hold the row, kept as bf16 (every value the statistics and the
+// output read is bf16-representable: x itself, or the bf16-rounded residual), so 3 vectors
+// (hidden <= 6144, H3's 5376) fit 32 registers and eight rows per SM are in flight; 4 cover the
+// rest. All of a row's x / y loads are issued before anything is stored: the compiler cannot move
+// a load above a store to x_out (which it must assume may alias), and one round trip to DRAM per
+// row instead of one per vector is what keeps HBM busy.
+template <int kVec, int kMinBlocks>
+__global__ void __launch_bounds__(kThreads, kMinBlocks) norm_modulate_kernel(const NormParams p) {
   __shared__ float red[kThreads / 32 + 1];
   const long long r = blockIdx.x;
   const int m = p.seg_row[r];
   const int n_vec = p.hidden >> 3;
-  float v[kVec][8];
+  const bool res = p.y != nullptr && m >= 0;
+  uint4 v[kVec], yv[kVec];
+#pragma unroll
+  for (int i = 0; i < kVec; ++i) {
+    const int c = threadIdx.x + i * kThreads;
+    if (c < n_vec) {
+      v[i] = *reinterpret_cast<const uint4*>(p.x + r * p.x_stride + 8 * c);
+      if (res) yv[i] = *reinterpret_cast<const uint4*>(p.y + r * p.y_stride + 8 * c);
+    }
+  }
   float s = 0.f;
 #pragma unroll
   for (int i = 0; i < kVec; ++i) {
     const int c = threadIdx.x + i * kThreads;
     if (c < n_vec) {
-      unpack8(*reinterpret_cast<const uint4*>(p.x + r * p.x_stride + 8 * c), v[i]);
-      if (p.y != nullptr && m >= 0) {
-        float y[8], g[8];
-        unpack8(*reinterpret_cast<const uint4*>(p.y + r * p.y_stride + 8 * c), y);
+      if (res) {
+        float a[8], y[8], g[8];
+        unpack8(v[i], a);
+        unpack8(yv[i], y);
         unpack8(*reinterpret_cast<const uint4*>(p.gate + m * p.mod_stride + 8 * c), g);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[i][e] = rb(v[i][e] + rb(g[e] * y[e]));
+        for (int e = 0; e < 8; ++e) a[e] = rb(a[e] + rb(g[e] * y[e]));
+        v[i] = pack8(a);
       }
-      if (p.x_out != nullptr) *reinterpret_cast<uint4*>(p.x_out + r * p.x_out_stride + 8 * c) = pack8(v[i]);
+      if (p.x_out != nullptr) *reinterpret_cast<uint4*>(p.x_out + r * p.x_out_stride + 8 * c) = v[i];
+      float f[8];
+      unpack8(v[i], f);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) s += v[i][e];
+      for (int e = 0; e < 8; ++e) s += f[e];
     }
   }
   const float mean = block_sum(s, red) / float(p.hidden);
@@ -113,9 +130,11 @@ __global__ void __launch_bounds__(kThreads, kVec == 3 ? 6 : 4) norm_modulate_ker
   for (int i = 0; i < kVec; ++i) {
     const int c = threadIdx.x + i * kThreads;
     if (c < n_vec) {
+      float f[8];
+      unpack8(v[i], f);
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const float d = v[i][e] - mean;
+        const float d = f[e] - mean;
         q += d * d;
       }
     }
@@ -125,9 +144,10 @@ __global__ void __launch_bounds__(kThreads, kVec == 3 ? 6 : 4) norm_modulate_ker
   for (int i = 0; i < kVec; ++i) {
     const int c = threadIdx.x + i * kThreads;
     if (c < n_vec) {
-      float o[8];
+      float o[8], f[8];
+      unpack8(v[i], f);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] = rb((v[i][e] - mean) * rstd);
+      for (int e = 0; e < 8; ++e) o[e] = rb((f[e] - mean) * rstd);
       if (m >= 0) {
         float sh[8], sc[8];
         unpack8(*reinterpret_cast<const uint4*>(p.shift + m * p.mod_stride + 8 * c), sh);
@@ -204,9 +224,9 @@ extern "C" int h3_norm_modulate(const void* x, int64_t x_row_stride, const void*
   p.hidden = (int)hidden;
   p.eps = eps;
   if (hidden <= 8 * kThreads * 3)
-    norm_modulate_kernel<3><<<(unsigned)rows, kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
+    norm_modulate_kernel<3, 8><<<(unsigned)rows, kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
   else
-    norm_modulate_kernel<kMaxVec><<<(unsigned)rows, kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
+    norm_modulate_kernel<kMaxVec, 6><<<(unsigned)rows, kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
   return cudaGetLastError() == cudaSuccess ? H3_OK : H3_ERR_LAUNCH;
 }
 
