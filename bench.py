@@ -628,7 +628,7 @@ def vendor_attention(x, rope, ones, eps, S, our_ms):
 def run_blocks_bench(args, rank, W, dev, sampler, max_over_ranks, sync_all):
     """Config 3: the 50-block MiniMax-H3 denoiser forward (run_blocks) through the installed runtime,
     as the reference's full-step harness measures it (harness/sp_full_step.py:48-93): hidden 5376,
-    56x128 heads, SwiGLU 14336, AdaLN from a sinusoidal t=500 embedding, bf16 weights ~N(0, 0.02),
+    56x128 heads, SwiGLU 14336, AdaLN from a sinusoidal t=500 embedding, bf16 weights and biases ~N(0, 0.02),
     the packed [512 | 1024 | 1464 | 39000] sequence of x ~N(0, 1). Returns the run_blocks record."""
     import h3_model as M
     import h3attn
@@ -638,11 +638,13 @@ def run_blocks_bench(args, rank, W, dev, sampler, max_over_ranks, sync_all):
     S = args.rb_seq
     blocks = args.rb_blocks
     model = M.MiniMaxH3Model(n_blocks=blocks, dtype=torch.bfloat16, device=dev)
-    g = torch.Generator(device=dev).manual_seed(3)  # the same weights on every rank
+    g = torch.Generator(device=dev).manual_seed(3)  # the same parameters on every rank
     with torch.no_grad():
         for m in model.modules():
             if isinstance(m, torch.nn.Linear):
                 m.weight.normal_(0.0, 0.02, generator=g)
+                if m.bias is not None:  # nn.Linear's default bias init would differ between ranks
+                    m.bias.normal_(0.0, 0.02, generator=g)
     segs = [(a, min(b, S), r) for a, b, r in M.H3_SEGMENTS if a < S]
     h = torch.randn((S, M.HIDDEN), generator=torch.Generator(device=dev).manual_seed(4), device=dev).to(torch.bfloat16)
     t_emb = M.timestep_embedding(torch.full((len(segs),), 500.0, device=dev)).to(torch.bfloat16)
