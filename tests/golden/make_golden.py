@@ -1,6 +1,6 @@
 """Generate the golden vectors in tests/golden/ by running the REFERENCE's own code.
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py --ref <checkout of shi3z/MinimaxH3-on-A100-x4>
 
 Runs here (CPU, gloo ranks); the GPU box never needs the reference. It imports
 harness/sp_runtime.py from the reference checkout (read-only) with the test stub `comfy`
@@ -160,7 +160,7 @@ def host_golden(ref_root, out_dir):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="path of a read-only checkout of the reference project")
     args = ap.parse_args()
     out_dir = HERE
     host_golden(args.ref, out_dir)
