@@ -81,6 +81,30 @@ def test_rows_independent(cuda_dev):
     assert torch.equal(part, full[300:700])
 
 
+def test_many_rows_and_in_place(cuda_dev):
+    """Thousands of rows per call give the same bits as row subsets, and x_out / h may be x itself
+    (a row is read completely before any of it is written)."""
+    import h3attn
+    import h3_model as M
+    x, y, (shift, scale, gate, _, _, _), segs = _setup(cuda_dev, rows=9001, seed=5)
+    seg = h3attn.segment_rows(segs, x.shape[0], cuda_dev)
+    x1 = torch.empty_like(x)
+    out = h3attn.norm_modulate(x, shift, scale, seg, 1e-6, y=y, gate=gate, x_out=x1)
+    part = h3attn.norm_modulate(x[4000:4100].contiguous(), shift, scale, seg[4000:4100].contiguous(), 1e-6,
+                                y=y[4000:4100].contiguous(), gate=gate)
+    xi = x.clone()
+    h_in = h3attn.norm_modulate(xi, shift, scale, seg, 1e-6, y=y, gate=gate, x_out=xi)  # residual in place
+    xh = x.clone()
+    h3attn.norm_modulate(xh, shift, scale, seg, 1e-6, out=xh)                           # h over x
+    plain = h3attn.norm_modulate(x, shift, scale, seg, 1e-6)
+    torch.cuda.synchronize()
+    h3attn.check_status()
+    assert torch.equal(x1, M._mod_gate(x, gate, y, segs))
+    assert torch.equal(part, out[4000:4100])
+    assert torch.equal(xi, x1) and torch.equal(h_in, out)
+    assert torch.equal(xh, plain)
+
+
 @pytest.mark.parametrize("hidden", [8, 1000, 1024, 8192])
 def test_widths(cuda_dev, hidden):
     import h3attn

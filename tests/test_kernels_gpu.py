@@ -148,6 +148,39 @@ def test_pack_bit_exact(cuda_dev, world):
     assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
 
 
+@pytest.mark.parametrize("S,H,world,head_major", [
+    (1, 3, 1, False),        # one token, q/k rows fewer than one step of the lane groups
+    (16, 8, 2, False),
+    (2369, 12, 2, False),    # 2 * 12 q/k rows: a partial last step of the row walk
+    (5003, 56, 8, True),     # the H3 head count, head-major layout, several grid-stride passes
+    (4099, 56, 4, False),
+])
+def test_pack_strided_inputs_bit_exact(cuda_dev, S, H, world, head_major):
+    """Padded input rows and rope rows, head counts that leave partial steps of the kernel's row walk,
+    token counts beyond one grid-stride pass and the head-major layout all give the oracle's bits."""
+    import h3attn
+    rng = np.random.default_rng(S + H)
+    qkv = O.bf16_round(rng.standard_normal((S, 3, H, 128), dtype=np.float32) * 2)
+    qw = O.bf16_round(1 + 0.1 * rng.standard_normal(128, dtype=np.float32))
+    kw = O.bf16_round(1 + 0.1 * rng.standard_normal(128, dtype=np.float32))
+    rope = O.rope_table(S, pos0=11)[0]
+    # rows padded past the three column blocks, rope rows padded past 256 floats
+    x = torch.zeros((S, 3 * H * 128 + 64), dtype=torch.bfloat16, device=cuda_dev)
+    x[:, :3 * H * 128] = _bf16(qkv.reshape(S, 3 * H * 128), cuda_dev)
+    q, k, v = x[:, :H * 128], x[:, H * 128:2 * H * 128], x[:, 2 * H * 128:3 * H * 128]
+    rope_pad = torch.zeros((S, 320), dtype=torch.float32, device=cuda_dev)
+    rope_pad[:, :256] = torch.from_numpy(rope.reshape(S, 256)).to(cuda_dev)
+    out = h3attn.qknorm_rope_pack(q, k, v, rope_pad[:, :256].view(S, 64, 2, 2), _bf16(qw, cuda_dev),
+                                  _bf16(kw, cuda_dev), 1e-6, world, head_major=head_major)
+    torch.cuda.synchronize()
+    h3attn.check_status()
+    if head_major:  # [hl, world, 3, S, D] -> [world, 3, hl, S, D]
+        out = out.permute(1, 2, 0, 3, 4)
+    ref = O.qknorm_rope_pack(qkv[:, 0], qkv[:, 1], qkv[:, 2], rope, qw, kw, 1e-6, world)
+    got = out.float().cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
 def test_pack_no_rope_no_weight(cuda_dev):
     import h3attn
     S, H = 33, 4
