@@ -370,6 +370,65 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         barrier(buf["flag"], timed)
         return buf["o"]
 
+    ce_bufs, ce_step, ce_streams = None, [0], None
+    if W > 1 and args.overlap == "ce":
+        import sp_runtime
+        ce_bufs = sp_runtime._peer_buffers(sl, H, D, dev, slots=2)
+        ce_streams = [torch.cuda.Stream() for _ in range(W)]
+        for b in ce_bufs:  # every rank's buffer bases, on the host
+            b["qkv_base"] = b["qkv_ptrs"].tolist()
+            b["o_base"] = [p - rank * hl * D * 2 for p in b["o_ptrs"].tolist()]
+
+    def layer_ce(x, out=None, timed=False):
+        """The same layer with both exchanges done by the copy engines: the pack writes the usual
+        send buffer, then one 2-D copy per destination rank puts this rank's q/k/v rows straight into
+        that rank's attention input [3][H/W][S][D] (rows rank*Sl...), and one contiguous copy per
+        destination puts this rank's attention output heads into that rank's [H][Sl][D] out_proj
+        input; the copies to different ranks run on their own streams, and a stream-ordered barrier
+        follows each exchange. No unpack kernel runs on the receive side of the q/k/v exchange."""
+        buf = ce_bufs[ce_step[0] % 2]
+        ce_step[0] += 1
+        cur = torch.cuda.current_stream()
+        q, k, v = x.split(H * D, dim=-1)
+        send = h3attn.qknorm_rope_pack(q, k, v, rope, ones, ones, eps, W)  # [W, 3, hl, sl, D]
+        if timed:
+            a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+        row = sl * D * 2
+        for d in range(W):
+            st = ce_streams[d]
+            st.wait_stream(cur)
+            h3attn.copy_2d(buf["qkv_base"][d] + rank * row, S_pad * D * 2, send[d].data_ptr(), row, row, 3 * hl,
+                           stream=st)
+        for st in ce_streams:
+            cur.wait_stream(st)
+        dist.all_reduce(buf["flag"])  # every rank's rows have landed
+        if timed:
+            b_.record()
+            ev_a2a.append((a, b_, send.numel() * 2 * (W - 1) // W))
+        qkvh = buf["qkv"]
+        if timed:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+        o_send = h3attn.attention(qkvh[0], qkvh[1], qkvh[2], s_kv=S, layout="send", world=W)  # [W, hl, sl, D]
+        if timed:
+            e1.record()
+            ev_att.append((e0, e1))
+            a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+        blk = hl * sl * D * 2
+        for d in range(W):
+            st = ce_streams[d]
+            st.wait_stream(cur)
+            h3attn.copy_2d(buf["o_base"][d] + rank * blk, blk, o_send[d].data_ptr(), blk, blk, 1, stream=st)
+        for st in ce_streams:
+            cur.wait_stream(st)
+        dist.all_reduce(buf["flag"])  # every rank's heads for this rank have landed
+        if timed:
+            b_.record()
+            ev_a2a.append((a, b_, o_send.numel() * 2 * (W - 1) // W))
+        return h3attn.head_to_seq_unpack(buf["o"].view(H, sl, D), out=out)
+
     def barrier(flag, timed):
         if timed:
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -385,6 +444,8 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         heads_per_launch = 1
     if W > 1 and args.overlap == "peer":
         layer = layer_peer  # noqa: F811
+    if W > 1 and args.overlap == "ce":
+        layer = layer_ce  # noqa: F811
 
     def sync_all():
         torch.cuda.synchronize()
@@ -542,7 +603,8 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     traffic = profiled_traffic("attn_fwd_s8192_h56_full.md", S, hl)
     # our kernels per step: pack, attention (W=1); + seq->head unpack and head->seq unpack (W>1),
     # the unpack and attention once per local head when pipelined by heads
-    per_step = 2 if W == 1 or peer_bufs is not None else (4 if heads_per_launch == hl else 2 + 2 * hl)
+    per_step = 2 if W == 1 or peer_bufs is not None else (
+        3 if ce_bufs is not None else (4 if heads_per_launch == hl else 2 + 2 * hl))
     launches = per_step * B * args.steps
     e2e_bound_ms = max(ms, h2d_alone, d2h_alone)
     line = {
@@ -575,8 +637,9 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
                        "frac_of_step": a2a_ms / ms}
     elif W > 1:
         gbs = a2a_bytes / (a2a_ms * 1e-3) / 1e9
-        key = "exposed_ms_per_step" if args.overlap == "none" else "comm_stream_ms_per_step_overlapped"
+        key = "exposed_ms_per_step" if args.overlap in ("none", "ce") else "comm_stream_ms_per_step_overlapped"
         line["a2a"] = {key: a2a_ms, "bytes_sent_per_gpu_per_step": a2a_bytes,
+                       "mode": "copy engines into peers' buffers + barrier" if args.overlap == "ce" else "NCCL all_to_all_single",
                        "achieved_gbs_per_gpu": gbs, "frac_of_nvlink": gbs / NVLINK_GBS,
                        "nvlink_ref": f"{NVLINK_GBS:.0f} GB/s per direction per GPU (measured peer copy)",
                        "frac_of_step": a2a_ms / ms}
@@ -780,8 +843,9 @@ def main():
     ap.add_argument("--no-vendor", action="store_true", help="skip timing torch SDPA at N=1")
     ap.add_argument("--no-numa-bind", action="store_true", help="leave host buffers wherever the OS puts them")
     ap.add_argument("--batch", type=int, default=1, help="independent sequences per step (config 4: 2)")
-    ap.add_argument("--overlap", default="none", choices=["none", "heads", "peer"],
-                    help="W>1: exchanges pipelined head by head, or fused into the kernels over peer memory")
+    ap.add_argument("--overlap", default="none", choices=["none", "heads", "peer", "ce"],
+                    help="W>1: exchanges pipelined head by head, fused into the kernels over peer memory, "
+                         "or done by the copy engines straight into peers' buffers")
     ap.add_argument("--rb-blocks", type=int, default=50, help="config 3 run_blocks forward depth (0: skip)")
     ap.add_argument("--rb-seq", type=int, default=42000)
     ap.add_argument("--rb-steps", type=int, default=2, help="timed run_blocks forwards")

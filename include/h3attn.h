@@ -239,6 +239,16 @@ int h3_attn_layer_noalloc(const void* qkv, int64_t qkv_row_stride, const float* 
 /* Synchronise `stream`, then return the status word's value (>= 0), or H3_ERR_CUDA. */
 int h3_status_read(const int32_t* status, void* stream);
 
+/* Copy-engine exchange step: `rows` rows of `width` bytes from src (row pitch src_pitch bytes) to
+ * dst (row pitch dst_pitch bytes), ordered on `stream`; either side may be a peer GPU's memory
+ * mapped into this process (CUDA IPC, cuMem or torch symmetric memory). One call moves one rank's
+ * chunk of an all-to-all straight into the destination's final layout (the attention input
+ * [3][H/W][S][128] at this rank's rows, or the out_proj input [H][S/W][128] at this rank's heads),
+ * the transfer the NCCL all-to-all plus unpack of harness/sp_runtime.py:67-77 performs. No kernel
+ * runs: the GPU's copy engines move the bytes. */
+int h3_copy_2d(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch, int64_t width, int64_t rows,
+               void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -298,6 +298,16 @@ extern "C" int h3_head_to_seq_unpack(const void* recv, void* out, int64_t n_head
   return cudaGetLastError() == cudaSuccess ? H3_OK : H3_ERR_LAUNCH;
 }
 
+extern "C" int h3_copy_2d(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch, int64_t width,
+                          int64_t rows, void* stream) {
+  if (!dst || !src) return H3_ERR_NULL;
+  if (width < 1 || rows < 1 || dst_pitch < width || src_pitch < width) return H3_ERR_SHAPE;
+  return cudaMemcpy2DAsync(dst, (size_t)dst_pitch, src, (size_t)src_pitch, (size_t)width, (size_t)rows,
+                           cudaMemcpyDefault, reinterpret_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? H3_OK
+             : H3_ERR_CUDA;
+}
+
 extern "C" int h3_status_read(const int32_t* status, void* stream) {
   if (!status) return H3_ERR_NULL;
   int32_t host = 0;

@@ -90,6 +90,8 @@ def lib() -> ctypes.CDLL:
         L.h3_qknorm_rope_pack_peer.restype = ctypes.c_int
         L.h3_attn_fwd_peer.argtypes = [vp] * 5 + [i64] * 11 + [ctypes.c_float, i32p, vp]
         L.h3_attn_fwd_peer.restype = ctypes.c_int
+        L.h3_copy_2d.argtypes = [vp, i64, vp, i64, i64, i64, vp]
+        L.h3_copy_2d.restype = ctypes.c_int
         L.h3_status_read.argtypes = [i32p, vp]
         L.h3_status_read.restype = ctypes.c_int
         _lib = L
@@ -310,6 +312,16 @@ def seq_to_head_unpack(recv: torch.Tensor, out: torch.Tensor | None = None) -> t
                                      hl * W * sl * D, _stream())
     _check(rc, "h3_seq_to_head_unpack")
     return out
+
+
+def copy_2d(dst_ptr: int, dst_pitch: int, src_ptr: int, src_pitch: int, width: int, rows: int,
+            stream: torch.cuda.Stream | None = None) -> None:
+    """Copy-engine copy of `rows` rows of `width` bytes (pitches in bytes) on `stream` (default: the
+    current one); either address may be a peer GPU's mapped memory. Used for the all-to-all
+    exchanges of SP_OVERLAP=ce: each rank writes its chunk straight into every destination's
+    attention / out_proj input."""
+    st = (stream or torch.cuda.current_stream()).cuda_stream
+    _check(lib().h3_copy_2d(dst_ptr, dst_pitch, src_ptr, src_pitch, width, rows, st), "h3_copy_2d")
 
 
 def head_to_seq_unpack(recv: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:

@@ -72,6 +72,13 @@ def test_pack_rejects_bad_arguments_before_launch(L):
     assert L.h3_qknorm_rope_pack(*bad) == -4
 
 
+def test_copy_2d_rejects_bad_arguments_before_any_copy(L):
+    p = ctypes.c_void_p(0x1000)
+    assert L.h3_copy_2d(None, 256, p, 256, 256, 4, None) == -1      # no destination
+    assert L.h3_copy_2d(p, 128, p, 256, 256, 4, None) == -3         # destination pitch below the row width
+    assert L.h3_copy_2d(p, 256, p, 256, 256, 0, None) == -3         # no rows
+
+
 def test_unpack_rejects_bad_arguments_before_launch(L):
     p = ctypes.c_void_p(0x1000)
     assert L.h3_seq_to_head_unpack(None, p, 2, 2, 8, 3, 0, 0, 0, None) == -1
