@@ -12,6 +12,7 @@ Same module API and behaviour, B200 data path underneath:
   env SP_TIMING=1, SP_OVERLAP=1, SP_PIECES=N                           (ref :32, :133, :265)
   env SP_OVERLAP=heads         head-by-head all-to-all / attention pipelining (this build)
   env SP_OVERLAP=peer          all-to-alls fused into pack / attention over peer memory (this build)
+  env SP_OVERLAP=ce            all-to-alls as copy-engine copies into peers' final buffers (this build)
 
 What differs, by design:
   * The attention layer runs on libh3attn.so (sm_100a): one fused kernel does the q/k
@@ -478,6 +479,73 @@ def _sp_attn_forward_peer(self, x, rope_freqs=None, transformer_options={}):
         return O.linear(buf["o"], w_out) if w_out is not None else self.out_proj(buf["o"].clone())
 
 
+_ce_streams = {}
+
+
+def _ce_copies(bases, offset, dst_pitch, chunks, width, rows, dev):
+    """One copy-engine copy per destination rank d: `rows` rows of `width` bytes from chunks[d] to
+    bases[d] + offset (row pitch dst_pitch), each on its own side stream ordered after the current
+    stream's work; the current stream then waits for all of them."""
+    cur = torch.cuda.current_stream()
+    streams = _ce_streams.get(str(dev))
+    if streams is None:
+        streams = _ce_streams[str(dev)] = [torch.cuda.Stream(device=dev) for _ in range(WORLD)]
+    for d in range(WORLD):
+        st = streams[d]
+        st.wait_stream(cur)
+        chunks[d].record_stream(st)
+        ops().copy_2d(bases[d] + offset, dst_pitch, chunks[d].data_ptr(), width, width, rows, stream=st)
+    for st in streams:
+        cur.wait_stream(st)
+
+
+def _sp_attn_forward_ce(self, x, rope_freqs=None, transformer_options={}):
+    """Same math with both all-to-alls done by the GPU's copy engines (this build's SP_OVERLAP=ce):
+    the pack writes the usual send buffer; one 2-D copy per destination rank puts this rank's q/k/v
+    rows straight into that rank's attention input [3][H/W][W*s][D] (symmetric memory, rows
+    RANK*s...), and one contiguous copy per destination puts this rank's attention output heads into
+    that rank's [H][s][D] out_proj input, which out_proj reads in place. No kernel spends SMs on the
+    exchanges and no unpack runs; a stream-ordered barrier follows each exchange. Bit-identical to
+    the blocking path."""
+    if not _SP_ACTIVE:
+        return _orig_attn_forward(self, x, rope_freqs=rope_freqs, transformer_options=transformer_options)
+    if WORLD == 1:
+        return _sp_attn_forward(self, x, rope_freqs=rope_freqs, transformer_options=transformer_options)
+    O = ops()
+    s = x.shape[0]
+    H, D, W = self.heads, self.head_dim, WORLD
+    hl = H // W
+    buf = _peer_buffers(s, H, D, x.device)[0]
+    if "qkv_base" not in buf:  # every rank's buffer bases, on the host
+        buf["qkv_base"] = buf["qkv_ptrs"].tolist()
+        buf["o_base"] = [p - RANK * hl * D * 2 for p in buf["o_ptrs"].tolist()]
+    S_pad = W * s
+    s_kv = _SP_REAL_S if (_SP_REAL_S is not None and _SP_REAL_S < S_pad) else S_pad
+    with _span("qkv"):
+        w_qkv = _gemm_weight(self.qkv_proj, x)
+        qkv = O.linear(x, w_qkv) if w_qkv is not None else self.qkv_proj(x)
+        q, k, v = qkv.split(H * D, dim=-1)
+        rope, qw, kw = _norm_inputs(self, x, rope_freqs)
+        send = O.qknorm_rope_pack(q, k, v, rope, qw, kw, self.q_norm.eps, W)  # [W, 3, H/W, s, D]
+    with _span("a2a_fwd"):
+        row = s * D * 2
+        _ce_copies(buf["qkv_base"], RANK * row, S_pad * D * 2, send, row, 3 * hl, x.device)
+        _peer_barrier(buf["flag"])  # every rank's q/k/v rows have landed
+    with _span("fa2_local"):
+        qkvh = buf["qkv"]
+        o_send = O.attention(qkvh[0], qkvh[1], qkvh[2], s_kv=s_kv, layout="send", world=W)  # [W, H/W, s, D]
+    with _span("a2a_inv"):
+        blk = hl * s * D * 2
+        _ce_copies(buf["o_base"], RANK * blk, blk, o_send, blk, 1, x.device)
+        _peer_barrier(buf["flag"])  # every rank's output heads for this rank have landed
+    with _span("out_proj"):
+        o_heads = buf["o"].view(H, s, D)
+        w_out = _gemm_weight(self.out_proj, x)
+        if w_out is not None:
+            return O.linear(o_heads, w_out)  # reads [H, s, D] as [s, H*D] in place
+        return self.out_proj(O.head_to_seq_unpack(o_heads))
+
+
 def _shard_segments(segs, lo, hi):
     out = []
     for a, b, row in segs:
@@ -628,13 +696,13 @@ def install(module=None):
     mode = os.environ.get("SP_OVERLAP", "0")
     overlap = mode == "1"
     module.Attention.forward = {"1": _sp_attn_forward_overlap, "heads": _sp_attn_forward_heads,
-                                "peer": _sp_attn_forward_peer}.get(mode, _sp_attn_forward)
+                                "peer": _sp_attn_forward_peer, "ce": _sp_attn_forward_ce}.get(mode, _sp_attn_forward)
     module.MiniMaxH3Model.run_blocks = _sp_run_blocks
     if _orig_mlp_forward is not None:
         module.MLP.forward = _sp_mlp_forward
     if RANK == 0:
-        mode = f"overlap(P={_PIECES})" if overlap else {"heads": "overlap(heads)", "peer": "fused exchanges (peer)"}.get(
-            mode, "blocking")
+        mode = f"overlap(P={_PIECES})" if overlap else {"heads": "overlap(heads)", "peer": "fused exchanges (peer)",
+                                                         "ce": "copy-engine exchanges"}.get(mode, "blocking")
         print(f"[sp_runtime] installed (WORLD={WORLD}) - run_blocks + Ulysses attention patched [{mode}]"
               + (" [SP_TIMING]" if _TIMING else ""), flush=True)
 

@@ -46,7 +46,7 @@ def _worker(rank, world, port, S, out_dir, overlap):
     os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port),
                       LOCAL_RANK=str(rank))
     if overlap:
-        os.environ["SP_OVERLAP"] = overlap  # "1": token pieces, "heads": head by head
+        os.environ["SP_OVERLAP"] = overlap  # "1": token pieces, "heads": head by head, "peer" / "ce": exchanges
     import sp_runtime
     import h3attn
     sp_runtime.init(timeout_s=120)
@@ -78,8 +78,8 @@ def _run(world, S, out_dir, overlap=None):
 
 
 @pytest.mark.parametrize("world,S,overlap", [(2, 1001, None), (2, 1024, "1"), (2, 1001, "heads"), (2, 1001, "peer"),
-                                             (4, 1003, "heads"), (4, 1003, None), (8, 1000, None), (8, 1000, "heads"),
-                                             (8, 1000, "peer")])
+                                             (2, 1001, "ce"), (4, 1003, "heads"), (4, 1003, None), (4, 1003, "ce"),
+                                             (8, 1000, None), (8, 1000, "heads"), (8, 1000, "peer"), (8, 1000, "ce")])
 def test_run_blocks_bit_exact_across_world(world, S, overlap, tmp_path):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
