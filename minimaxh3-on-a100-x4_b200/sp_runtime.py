@@ -482,6 +482,17 @@ def _sp_attn_forward_peer(self, x, rope_freqs=None, transformer_options={}):
 _ce_streams = {}
 
 
+def _ce_geometry(s: int, H: int, D: int, W: int, rank: int) -> dict:
+    """Byte geometry of this rank's two copy-engine exchanges, the same for every destination:
+    qkv: (offset into the destination's [3][H/W][W*s][D] attention input, its row pitch, bytes per
+         row, rows) -- row (t, h) of this rank's send chunk [3][H/W][s][D] lands at rows rank*s...;
+    o:   (offset into the destination's [H][s][D] out_proj input, bytes) -- this rank's H/W heads.
+    Elements are 2-byte bf16."""
+    hl = H // W
+    row = s * D * 2
+    return {"qkv": (rank * row, W * s * D * 2, row, 3 * hl), "o": (rank * hl * s * D * 2, hl * s * D * 2)}
+
+
 def _ce_copies(bases, offset, dst_pitch, chunks, width, rows, dev):
     """One copy-engine copy per destination rank d: `rows` rows of `width` bytes from chunks[d] to
     bases[d] + offset (row pitch dst_pitch), each on its own side stream ordered after the current
@@ -527,16 +538,17 @@ def _sp_attn_forward_ce(self, x, rope_freqs=None, transformer_options={}):
         q, k, v = qkv.split(H * D, dim=-1)
         rope, qw, kw = _norm_inputs(self, x, rope_freqs)
         send = O.qknorm_rope_pack(q, k, v, rope, qw, kw, self.q_norm.eps, W)  # [W, 3, H/W, s, D]
+    geo = _ce_geometry(s, H, D, W, RANK)
     with _span("a2a_fwd"):
-        row = s * D * 2
-        _ce_copies(buf["qkv_base"], RANK * row, S_pad * D * 2, send, row, 3 * hl, x.device)
+        off, pitch, row, rows = geo["qkv"]
+        _ce_copies(buf["qkv_base"], off, pitch, send, row, rows, x.device)
         _peer_barrier(buf["flag"])  # every rank's q/k/v rows have landed
     with _span("fa2_local"):
         qkvh = buf["qkv"]
         o_send = O.attention(qkvh[0], qkvh[1], qkvh[2], s_kv=s_kv, layout="send", world=W)  # [W, H/W, s, D]
     with _span("a2a_inv"):
-        blk = hl * s * D * 2
-        _ce_copies(buf["o_base"], RANK * blk, blk, o_send, blk, 1, x.device)
+        off, blk = geo["o"]
+        _ce_copies(buf["o_base"], off, blk, o_send, blk, 1, x.device)
         _peer_barrier(buf["flag"])  # every rank's output heads for this rank have landed
     with _span("out_proj"):
         o_heads = buf["o"].view(H, s, D)

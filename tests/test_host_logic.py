@@ -130,3 +130,40 @@ def test_timeline_books_host_spans_by_category():
         pass
     tot = tl.totals()
     assert set(tot) == {"qkv", "gather"} and tot["qkv"] >= 9.0 and tot["gather"] >= 0.0
+
+
+@pytest.mark.parametrize("world,H,s", [(2, 4, 5), (4, 8, 3), (8, 56, 2)])
+def test_copy_engine_exchange_geometry_reproduces_the_all_to_alls(world, H, s):
+    """SP_OVERLAP=ce: every rank copies rows of its send chunks straight into each destination's
+    buffers with the geometry _ce_geometry plans. Replayed on byte buffers for all ranks, the copies
+    must leave each rank's attention input equal to all-to-all + seq->head unpack of the blocking
+    path, and each rank's out_proj input equal to the head->seq all-to-all (oracle layouts)."""
+    import numpy as np
+    import sp_runtime
+    from oracle import h3_oracle as O
+
+    D, hl = 2, H // world  # a short head_dim keeps the replay small; the geometry is per element size
+    rng = np.random.default_rng(world * 100 + H)
+    sends = [rng.integers(0, 2 ** 16, size=(world, 3, hl, s, D), dtype=np.uint16) for _ in range(world)]
+    attn_in = [np.zeros(3 * hl * world * s * D, dtype=np.uint16) for _ in range(world)]
+    o_sends = [rng.integers(0, 2 ** 16, size=(world, hl, s, D), dtype=np.uint16) for _ in range(world)]
+    o_in = [np.zeros(H * s * D, dtype=np.uint16) for _ in range(world)]
+    for r in range(world):
+        geo = sp_runtime._ce_geometry(s, H, D, world, r)
+        off, pitch, width, rows = geo["qkv"]
+        o_off, o_bytes = geo["o"]
+        for d in range(world):
+            src = sends[r][d].reshape(-1).view(np.uint8)
+            dst = attn_in[d].view(np.uint8)
+            for i in range(rows):
+                dst[off + i * pitch:off + i * pitch + width] = src[i * width:(i + 1) * width]
+            o_in[d].view(np.uint8)[o_off:o_off + o_bytes] = o_sends[r][d].reshape(-1).view(np.uint8)
+    for d in range(world):
+        # blocking path: rank d receives chunk d of every source rank, then unpacks to [3][hl][W*s][D]
+        recv = np.stack([sends[r][d] for r in range(world)])
+        assert np.array_equal(attn_in[d].reshape(3, hl, world * s, D), O.seq_to_head_unpack(recv, world))
+    # head->seq: per-rank [1, hl, W*s, D] attention outputs -> per-rank [1, H, s, D]
+    o_full = [np.concatenate([o_sends[r][d] for d in range(world)], axis=1)[None] for r in range(world)]
+    want = O.a2a_head_to_seq(o_full)
+    for d in range(world):
+        assert np.array_equal(o_in[d].reshape(1, H, s, D), want[d])
